@@ -1,0 +1,108 @@
+/*
+ * phantom_attn.h - C ABI of the B200 (sm_100a) fused attention forward.
+ *
+ *   O = softmax(Q K^T / sqrt(d)) V      per (batch, head), online (running max / sum) softmax
+ *
+ * This is the drop-in boundary for the attention kernels of b4batunde/Phantom-A100. Every entry
+ * point below replaces one launcher of that project's `csrc/kernels/` layer (which returned a
+ * cudaError_t and took typed device pointers) with a plain C function: untyped device pointers,
+ * sizes, a dtype code and a CUDA stream. No torch types cross this boundary.
+ *
+ * Layout (all entry points): q, k, v, o are contiguous row-major (BH, N, d) device arrays, element
+ * ((bh * N) + i) * d + c, as in the reference (csrc/kernels/fused_tc.cuh:60,92). The library
+ * never writes q, k, v. o is written in full (rows < N) by the launch. Launches are asynchronous
+ * on `stream` (a cudaStream_t, NULL = legacy default stream) and run on the current device.
+ *
+ * Errors: every call returns PHANTOM_ATTN_OK or an error code; phantom_attn_last_error() returns a
+ * human-readable message for the last failing call on the calling thread. The message texts keep
+ * the substrings the reference tests match ("head dimension", "float16", "not compiled",
+ * "16-byte aligned", "shared memory"; reference csrc/common.cuh:27-33, attn_fused_tuned.cu:9-14).
+ *
+ * Device-side waits in the tensor-core kernel are bounded. A wait that expires (which only a
+ * hardware or programming fault can cause) makes the kernel stop early and record a non-zero
+ * status word on the device; phantom_attn_device_status() reads and clears it.
+ */
+#ifndef PHANTOM_ATTN_H_
+#define PHANTOM_ATTN_H_
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* dtype codes */
+#define PHANTOM_ATTN_F32 0
+#define PHANTOM_ATTN_F16 1
+#define PHANTOM_ATTN_BF16 2
+
+/* status codes */
+#define PHANTOM_ATTN_OK 0
+#define PHANTOM_ATTN_ERR_INVALID 1     /* bad pointer, shape, alignment or dtype             */
+#define PHANTOM_ATTN_ERR_UNSUPPORTED 2 /* configuration not compiled (head dim, tile, dtype)  */
+#define PHANTOM_ATTN_ERR_CUDA 3        /* a CUDA runtime or driver call failed                */
+#define PHANTOM_ATTN_ERR_DEVICE 4      /* a device-side bounded wait expired (status word)    */
+
+/* Library version, e.g. 10000 for 1.0.0. */
+int phantom_attn_version(void);
+
+/* Message for the last failing call on this thread ("" if none). Valid until the next call. */
+const char* phantom_attn_last_error(void);
+
+/*
+ * v4 replacement: fused attention on 5th-generation tensor cores (tcgen05.mma, TMEM accumulators,
+ * TMA-staged K/V ring). dtype PHANTOM_ATTN_F16 or PHANTOM_ATTN_BF16, head_dim 64 or 128, any
+ * seq_len >= 1, causal 0/1. fp32 accumulation, P rounded to the input dtype for the P.V product.
+ * Replaces attn::launch_fused_tc (reference csrc/kernels/fused_tc.cuh:187-196), which took
+ * (const __half* q, k, v, __half* o, int BH, int N, bool causal, cudaStream_t) with d fixed at 64
+ * and fp16 only; head_dim and dtype are explicit here because both are now selectable.
+ */
+int phantom_attn_fused_tc(const void* q, const void* k, const void* v, void* o, int BH, int N,
+                          int head_dim, int dtype, int causal, void* stream);
+
+/*
+ * v3.1/v3.2 replacement. (br, bc) must be one of the reference's compiled tiles (64,32) (64,64)
+ * (128,32) (128,64), else PHANTOM_ATTN_ERR_UNSUPPORTED with "not compiled". On sm_100a the work
+ * runs on the tensor-core kernel above (its tile is fixed by the tcgen05 instruction shape); the
+ * tile and double_buffer arguments are validated for interface compatibility only.
+ * Replaces attn::launch_fused_tuned (reference csrc/kernels/fused_tuned.cuh:212-228).
+ */
+int phantom_attn_fused_tuned(const void* q, const void* k, const void* v, void* o, int BH, int N,
+                             int head_dim, int dtype, int causal, int double_buffer, int br, int bc,
+                             void* stream);
+
+/*
+ * v3 replacement: fused online-softmax attention on CUDA cores with fp32 arithmetic, for fp32,
+ * fp16 and bf16 inputs and any head_dim in [1, 256]. Exact fp32 path (no tensor cores): meets the
+ * reference's 1e-4 fp32 tolerance. Replaces attn::launch_fused (reference
+ * csrc/kernels/fused.cuh:107-112), which compiled d == 64 only.
+ */
+int phantom_attn_fused(const void* q, const void* k, const void* v, void* o, int BH, int N,
+                       int head_dim, int dtype, int causal, void* stream);
+
+/*
+ * v1 / v2 replacements (reference csrc/kernels/naive.cuh:56-64, tiled.cuh:109-117). The reference
+ * materialised the BH x N x N fp32 score matrix in a caller-provided workspace; on sm_100a the same
+ * result comes from the fused CUDA-core kernel, so no workspace argument exists.
+ */
+int phantom_attn_naive(const void* q, const void* k, const void* v, void* o, int BH, int N,
+                       int head_dim, int dtype, int causal, void* stream);
+int phantom_attn_tiled(const void* q, const void* k, const void* v, void* o, int BH, int N,
+                       int head_dim, int dtype, int causal, void* stream);
+
+/*
+ * Reads and clears the device status word of the current device (synchronises the device).
+ * *status = 0 when every kernel since the last call finished normally; otherwise a bit set of
+ * where a bounded wait expired. No counterpart in the reference (its kernels had no waits).
+ */
+int phantom_attn_device_status(int* status);
+
+/*
+ * Number of kernel launches made by this library on the calling thread since the last reset
+ * (reset = 1 clears it). Used by the benchmark to count the launches in a timed region.
+ */
+long long phantom_attn_launch_count(int reset);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PHANTOM_ATTN_H_ */

@@ -1,0 +1,412 @@
+// Fused attention forward on B200 5th-generation tensor cores (sm_100a).
+//
+//   O = softmax(Q K^T / sqrt(d)) V,   online softmax in the log2 domain
+//
+// Algorithm (same arithmetic contract as the reference's v4 kernel, csrc/kernels/fused_tc.cuh:45-179,
+// and its NumPy model cuda_attn/online_softmax_ref.py:27-63 with p_fp16=True): scores in fp32, a
+// running row max m and row sum l in fp32, P = exp2(S*log2e/sqrt(d) - m) rounded to the input dtype
+// for the P.V product while l sums the unrounded fp32 values, O accumulated in fp32 and divided by l
+// once at the end.
+//
+// B200 mapping (not a translation of the WMMA kernel):
+//   * One CTA owns two 128-row Q tiles (A, B) of one (batch, head) and streams K/V tiles of 128 keys.
+//   * Warp 9 (one thread) is the TMA producer: Q tiles once, then K_0, V_0, K_1, V_1, ... into a ring
+//     of STAGES shared-memory slots (128-byte swizzle), completion tracked by mbarrier tx bytes.
+//   * Warp 8 (one thread) issues every tcgen05.mma: S_g = Q_g K_j^T (both operands in shared memory,
+//     fp32 accumulator in TMEM, 128 lanes x 128 columns) and O_g += P_g V_j (P read from TMEM,
+//     V from shared memory as an MN-major operand, accumulator in TMEM). Commits go to mbarriers.
+//   * Warps 0-3 / 4-7 are the softmax warpgroups of tiles A / B: thread t owns query row t = TMEM
+//     lane t, so the row max and row sum need no shuffles. Each thread loads its S row from TMEM,
+//     masks, takes the max, rescales its O row in TMEM only when the max grew by more than 2^8
+//     (exact: every P and l of a row use the same reference max), computes P with ex2, writes it
+//     back into the S columns as packed 16-bit pairs (the A operand of the next MMA), then arrives.
+//   * While one warpgroup runs its softmax the tensor core works on the other tile's MMAs.
+//   * TMEM: S_A [0,128), S_B [128,256), O_A [256,256+d), O_B [256+d,256+2d); P_g aliases S_g.
+//   * Every mbarrier wait is bounded; on expiry the CTA drains its in-flight copies and MMAs,
+//     frees TMEM, records the failure in the device status word and exits.
+#include <cuda.h>
+#include <math_constants.h>
+
+#include <mutex>
+
+#include "launchers.h"
+#include "sm100_ptx.cuh"
+#include "../../include/phantom_attn.h"
+
+namespace phantom {
+namespace tc {
+
+constexpr int BM = 128;  // query rows per Q tile = TMEM lanes
+constexpr int BN = 128;  // keys per K/V tile
+constexpr int MMA_WARP = 8;
+constexpr int TMA_WARP = 9;          // warps 10-11 complete the producer warpgroup and idle
+constexpr int NUM_THREADS = 384;
+// Register split (setmaxnreg): the kernel launches at 168 registers/thread (384 threads, 1 CTA/SM).
+// The producer warpgroup drops to 40 and the two softmax warpgroups rise to 232:
+// 128*(168-40) = 2*128*(232-168), so the increase is exactly covered by the release.
+constexpr int kRegsProducer = 40;
+constexpr int kRegsSoftmax = 232;
+constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale O only when the max grows by > 2^8
+
+// Status-word bits (which wait expired).
+constexpr int kErrTmaWait = 1, kErrMmaWait = 2, kErrSoftmaxWait = 4, kErrEpilogueWait = 8;
+
+template <int D>
+struct Cfg {
+  static constexpr int KBLK = D / 64;                // 64-element (128-byte) swizzle blocks across d
+  static constexpr int SUB_BYTES = BM * 128;         // one 64-column block of a 128-row tile
+  static constexpr int TILE_BYTES = BM * D * 2;      // one Q, K or V tile
+  static constexpr int STAGES = D == 128 ? 4 : 8;    // K/V ring slots
+  static constexpr int OFF_Q = 0;
+  static constexpr int OFF_KV = 2 * TILE_BYTES;
+  static constexpr int OFF_BAR = OFF_KV + STAGES * TILE_BYTES;
+  // barriers: q_full, kv_full[STAGES], kv_empty[STAGES], s_full[2], p_ready[2], o_done[2], drain
+  static constexpr int NUM_BARS = 1 + 2 * STAGES + 7;
+  static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;  // TMEM base address, abort flag
+  static constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;  // + slack to align the base to 1024
+  static constexpr uint32_t TMEM_COLS = 512;
+  static constexpr uint32_t T_S0 = 0, T_S1 = 128, T_O0 = 256, T_O1 = 256 + D;
+};
+
+__device__ __forceinline__ void ld128(uint32_t taddr, float (&s)[128]) {
+  uint32_t r[64];
+  tmem_ld64_wait(taddr, r);
+#pragma unroll
+  for (int i = 0; i < 64; ++i) s[i] = __uint_as_float(r[i]);
+  tmem_ld64_wait(taddr + 64, r);
+#pragma unroll
+  for (int i = 0; i < 64; ++i) s[64 + i] = __uint_as_float(r[i]);
+}
+
+template <int D, bool BF16>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+            const __grid_constant__ CUtensorMap tmV, uint16_t* __restrict__ O, int N, float scale_log2,
+            int causal, int* __restrict__ status) {
+  using C = Cfg<D>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sbase = smem_u32(smem);
+  const uint32_t bar0 = sbase + C::OFF_BAR;
+  auto q_full = [&]() { return bar0; };
+  auto kv_full = [&](int s) { return bar0 + 8u * (1 + s); };
+  auto kv_empty = [&](int s) { return bar0 + 8u * (1 + C::STAGES + s); };
+  auto s_full = [&](int g) { return bar0 + 8u * (1 + 2 * C::STAGES + g); };
+  auto p_ready = [&](int g) { return bar0 + 8u * (3 + 2 * C::STAGES + g); };
+  auto o_done = [&](int g) { return bar0 + 8u * (5 + 2 * C::STAGES + g); };
+  const uint32_t drain_bar = bar0 + 8u * (7 + 2 * C::STAGES);
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 4);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int bh = blockIdx.y;
+  const int n_qtiles = (N + BM - 1) / BM;
+  const int qblk = gridDim.x - 1 - blockIdx.x;  // heaviest (causal) blocks first
+  const int qt0 = 2 * qblk;
+  const bool has_b = qt0 + 1 < n_qtiles;
+  const int row0 = qt0 * BM;
+  const int kv_end = causal ? min(N, row0 + (has_b ? 2 * BM : BM)) : N;
+  const int n_kv = (kv_end + BN - 1) / BN;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full(), 1);
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(kv_full(s), 1);
+      mbar_init(kv_empty(s), 1);
+    }
+    for (int g = 0; g < 2; ++g) {
+      mbar_init(s_full(g), 1);
+      mbar_init(p_ready(g), 128);
+      mbar_init(o_done(g), 1);
+    }
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == MMA_WARP) {
+    tmem_alloc(smem_u32(tmem_holder), C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+
+  if (warp == TMA_WARP || warp >= MMA_WARP + 2) {
+    setmaxnreg_dec<kRegsProducer>();
+    if (warp == TMA_WARP && lane == 0) {
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV);
+      const int nq = has_b ? 2 : 1;
+      mbar_arrive_expect_tx(q_full(), nq * C::TILE_BYTES);
+      for (int g = 0; g < nq; ++g)
+        for (int c = 0; c < C::KBLK; ++c)
+          tma_load_3d(sbase + C::OFF_Q + g * C::TILE_BYTES + c * C::SUB_BYTES, &tmQ, q_full(), c * 64,
+                      row0 + g * BM, bh);
+      int issued = 0;
+      for (int t = 0; t < 2 * n_kv; ++t) {
+        const int s = t % C::STAGES, r = t / C::STAGES;
+        if (r > 0 && !mbar_wait(kv_empty(s), (r - 1) & 1, abort_flag, status, kErrTmaWait)) break;
+        mbar_arrive_expect_tx(kv_full(s), C::TILE_BYTES);
+        const CUtensorMap* m = (t & 1) ? &tmV : &tmK;
+        const int j = t >> 1;
+        for (int c = 0; c < C::KBLK; ++c)
+          tma_load_3d(sbase + C::OFF_KV + s * C::TILE_BYTES + c * C::SUB_BYTES, m, kv_full(s), c * 64, j * BN, bh);
+        issued = t + 1;
+      }
+      // Drain: every issued copy must land before this CTA's shared memory can be released.
+      mbar_wait_drain(q_full(), 0);
+      for (int t = (issued > C::STAGES ? issued - C::STAGES : 0); t < issued; ++t)
+        mbar_wait_drain(kv_full(t % C::STAGES), (t / C::STAGES) & 1);
+    }
+  } else if (warp == MMA_WARP) {
+    setmaxnreg_dec<kRegsProducer>();
+    if (lane == 0) {
+      constexpr uint32_t idesc_qk = idesc_f16(BF16, BM, BN, false);
+      constexpr uint32_t idesc_pv = idesc_f16(BF16, BM, D, true);
+      auto issue_qk = [&](int g, int stage) {
+        const uint32_t a0 = sbase + C::OFF_Q + g * C::TILE_BYTES;
+        const uint32_t b0 = sbase + C::OFF_KV + stage * C::TILE_BYTES;
+        const uint32_t d_t = tmem + (g ? C::T_S1 : C::T_S0);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * C::SUB_BYTES + (kk & 3) * 32;
+          mma_ss(d_t, smem_desc_sw128(a0 + off, 16, 1024), smem_desc_sw128(b0 + off, 16, 1024), idesc_qk,
+                 kk > 0 ? 1u : 0u);
+        }
+      };
+      auto issue_pv = [&](int g, int stage, bool acc) {
+        const uint32_t v0 = sbase + C::OFF_KV + stage * C::TILE_BYTES;
+        const uint32_t d_t = tmem + (g ? C::T_O1 : C::T_O0);
+        const uint32_t p_t = tmem + (g ? C::T_S1 : C::T_S0);
+#pragma unroll
+        for (int kk = 0; kk < BN / 16; ++kk)
+          mma_ts(d_t, p_t + kk * 8, smem_desc_sw128(v0 + kk * 2048, C::SUB_BYTES, 1024), idesc_pv,
+                 (acc || kk > 0) ? 1u : 0u);
+      };
+      const int ng = has_b ? 2 : 1;
+      bool ok = mbar_wait(q_full(), 0, abort_flag, status, kErrMmaWait);
+      int t = 0;  // index into the K0, V0, K1, V1, ... load sequence
+      if (ok) ok = mbar_wait(kv_full(0), 0, abort_flag, status, kErrMmaWait);
+      if (ok) {
+        tc_fence_after();
+        for (int g = 0; g < ng; ++g) {
+          issue_qk(g, 0);
+          mma_commit(s_full(g));
+        }
+        mma_commit(kv_empty(0));
+        t = 1;
+      }
+      for (int j = 0; ok && j < n_kv; ++j) {
+        // O_g += P_g V_j
+        const int sv = t % C::STAGES;
+        if (!(ok = mbar_wait(kv_full(sv), (t / C::STAGES) & 1, abort_flag, status, kErrMmaWait))) break;
+        for (int g = 0; g < ng && ok; ++g) {
+          if (!(ok = mbar_wait(p_ready(g), j & 1, abort_flag, status, kErrMmaWait))) break;
+          tc_fence_after();
+          issue_pv(g, sv, j > 0);
+          mma_commit(o_done(g));
+        }
+        if (!ok) break;
+        mma_commit(kv_empty(sv));
+        ++t;
+        if (j + 1 < n_kv) {
+          // S_g = Q_g K_{j+1}^T, once P_g (aliasing S_g) has been consumed by the PV product.
+          const int sk = t % C::STAGES;
+          if (!(ok = mbar_wait(kv_full(sk), (t / C::STAGES) & 1, abort_flag, status, kErrMmaWait))) break;
+          for (int g = 0; g < ng && ok; ++g) {
+            if (!(ok = mbar_wait(o_done(g), j & 1, abort_flag, status, kErrMmaWait))) break;
+            tc_fence_after();
+            issue_qk(g, sk);
+            mma_commit(s_full(g));
+          }
+          if (!ok) break;
+          mma_commit(kv_empty(sk));
+          ++t;
+        }
+      }
+      // Drain: all MMAs issued by this thread complete before TMEM is released.
+      mma_commit(drain_bar);
+      mbar_wait_drain(drain_bar, 0);
+    }
+  } else {
+    // Softmax warpgroups.
+    setmaxnreg_inc<kRegsSoftmax>();
+    const int g = warp >> 2;
+    const int r_local = threadIdx.x & 127;  // row within the Q tile = TMEM lane
+    if (g == 0 || has_b) {
+      const int tile_row0 = row0 + g * BM;
+      const int row = tile_row0 + r_local;
+      const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
+      const uint32_t t_s = tmem + lane_off + (g ? C::T_S1 : C::T_S0);
+      const uint32_t t_o = tmem + lane_off + (g ? C::T_O1 : C::T_O0);
+      float m_used = -CUDART_INF_F, l = 0.f;
+      bool ok = true;
+      for (int j = 0; j < n_kv; ++j) {
+        ok = mbar_wait(s_full(g), j & 1, abort_flag, status, kErrSoftmaxWait);
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok) break;
+        tc_fence_after();
+        float s[128];
+        ld128(t_s, s);
+        const int j0 = j * BN;
+        if (j0 + BN > N || (causal && j0 + BN - 1 > tile_row0)) {
+#pragma unroll
+          for (int c = 0; c < BN; ++c) {
+            const int col = j0 + c;
+            if (col >= N || (causal && col > row)) s[c] = -CUDART_INF_F;
+          }
+        }
+        float mx = s[0];
+#pragma unroll
+        for (int c = 1; c < BN; ++c) mx = fmaxf(mx, s[c]);
+        const float m_new = mx * scale_log2;
+        if (j == 0) {
+          m_used = m_new;
+        } else {
+          const bool need = m_new > m_used + kRescaleThreshold;
+          if (__any_sync(0xffffffffu, need)) {
+            float alpha = 1.f;
+            if (need) {
+              alpha = ex2(m_used - m_new);
+              m_used = m_new;
+            }
+            l *= alpha;
+#pragma unroll
+            for (int c = 0; c < D / 32; ++c) {
+              uint32_t r[32];
+              tmem_ld32_wait(t_o + c * 32, r);
+#pragma unroll
+              for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
+              tmem_st32(t_o + c * 32, r);
+            }
+          }
+        }
+        const float m_sub = m_used == -CUDART_INF_F ? 0.f : m_used;
+        float rowsum = 0.f;
+        uint32_t p_lo[32], p_hi[32];
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+          const float p0 = ex2(fmaf(s[2 * c], scale_log2, -m_sub));
+          const float p1 = ex2(fmaf(s[2 * c + 1], scale_log2, -m_sub));
+          const float p2 = ex2(fmaf(s[64 + 2 * c], scale_log2, -m_sub));
+          const float p3 = ex2(fmaf(s[64 + 2 * c + 1], scale_log2, -m_sub));
+          rowsum += (p0 + p1) + (p2 + p3);
+          p_lo[c] = pack2<BF16>(p0, p1);
+          p_hi[c] = pack2<BF16>(p2, p3);
+        }
+        l += rowsum;
+        tmem_st32(t_s, p_lo);
+        tmem_st32(t_s + 32, p_hi);
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(p_ready(g));
+      }
+      if (ok) {
+        ok = mbar_wait(o_done(g), (n_kv - 1) & 1, abort_flag, status, kErrEpilogueWait);
+        ok = __all_sync(0xffffffffu, ok);
+      }
+      if (ok) {
+        tc_fence_after();
+        const float inv_l = 1.f / l;
+        uint16_t* out = O + ((size_t)bh * N + row) * D;
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld32_wait(t_o + c * 32, r);
+          uint32_t w[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i)
+            w[i] = pack2<BF16>(__uint_as_float(r[2 * i]) * inv_l, __uint_as_float(r[2 * i + 1]) * inv_l);
+          if (row < N) {
+            uint4* dst = reinterpret_cast<uint4*>(out + c * 32);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) dst[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == MMA_WARP) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
+}  // namespace tc
+
+// ------------------------------------------------------------------------------------ host side
+namespace {
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// (d, N, BH) view of a contiguous (BH, N, d) 16-bit array; 64 x 128 x 1 boxes, 128-byte swizzle.
+// Rows past N read as zeros, per head.
+bool make_map(CUtensorMap* m, const void* base, int BH, int N, int d, bool bf16) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  const cuuint64_t dims[3] = {(cuuint64_t)d, (cuuint64_t)N, (cuuint64_t)BH};
+  const cuuint64_t strides[2] = {(cuuint64_t)d * 2, (cuuint64_t)N * d * 2};
+  const cuuint32_t box[3] = {64, (cuuint32_t)tc::BM, 1};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
+                  const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+template <int D, bool BF16>
+cudaError_t launch_t(const LaunchArgs& a, const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv) {
+  auto kern = tc::attn_fwd_tc<D, BF16>;
+  constexpr int smem = tc::Cfg<D>::SMEM_BYTES;
+  static bool attr_set[64] = {};  // per device
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    attr_set[dev] = true;
+  }
+  const int n_qtiles = (a.N + tc::BM - 1) / tc::BM;
+  const dim3 grid((n_qtiles + 1) / 2, a.BH);
+  const float scale_log2 = 1.4426950408889634f / sqrtf((float)D);
+  kern<<<grid, tc::NUM_THREADS, smem, a.stream>>>(mq, mk, mv, static_cast<uint16_t*>(a.o), a.N, scale_log2,
+                                                   a.causal ? 1 : 0, a.status);
+  note_launch();
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+size_t fused_tc_smem_bytes(int d) { return d == 64 ? tc::Cfg<64>::SMEM_BYTES : tc::Cfg<128>::SMEM_BYTES; }
+
+cudaError_t launch_fused_tc_sm100(const LaunchArgs& a) {
+  const bool bf16 = a.dtype == PHANTOM_ATTN_BF16;
+  CUtensorMap mq, mk, mv;
+  if (!make_map(&mq, a.q, a.BH, a.N, a.d, bf16) || !make_map(&mk, a.k, a.BH, a.N, a.d, bf16) ||
+      !make_map(&mv, a.v, a.BH, a.N, a.d, bf16))
+    return cudaErrorInvalidValue;
+  if (a.d == 64) return bf16 ? launch_t<64, true>(a, mq, mk, mv) : launch_t<64, false>(a, mq, mk, mv);
+  return bf16 ? launch_t<128, true>(a, mq, mk, mv) : launch_t<128, false>(a, mq, mk, mv);
+}
+
+}  // namespace phantom

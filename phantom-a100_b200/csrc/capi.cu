@@ -1,0 +1,218 @@
+// C ABI of the attention library (declared in include/phantom_attn.h). Validates arguments the way
+// the reference's torch glue did (csrc/common.cuh:27-40, attn_fused_tc.cu:5-19,
+// attn_fused_tuned.cu:5-21), keeps its error substrings, and dispatches to the sm_100a kernels.
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <mutex>
+#include <string>
+
+#include "launchers.h"
+#include "../../include/phantom_attn.h"
+
+namespace phantom {
+namespace {
+
+thread_local std::string g_last_error;
+thread_local long long g_launches = 0;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+int cuda_fail(const char* name, cudaError_t e) {
+  return fail(PHANTOM_ATTN_ERR_CUDA, "%s: CUDA error: %s", name, cudaGetErrorString(e));
+}
+
+constexpr int kMaxDevices = 64;
+std::mutex g_mu;
+int* g_status[kMaxDevices] = {};   // per-device status word (bounded-wait expiry bits)
+int g_cc[kMaxDevices] = {};        // per-device compute capability (major * 10 + minor), 0 = unknown
+int g_optin[kMaxDevices] = {};     // per-device opt-in shared memory per block
+
+struct Device {
+  int id = 0;
+  int cc = 0;
+  int optin = 0;
+  int* status = nullptr;
+};
+
+// Current device, its properties and its status word (allocated once per device, zeroed).
+int current_device(const char* name, Device* out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(name, e);
+  if (dev < 0 || dev >= kMaxDevices) return fail(PHANTOM_ATTN_ERR_INVALID, "%s: device %d out of range", name, dev);
+  std::lock_guard<std::mutex> lock(g_mu);
+  if (g_cc[dev] == 0) {
+    int major = 0, minor = 0, optin = 0;
+    if ((e = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev)) != cudaSuccess ||
+        (e = cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev)) != cudaSuccess ||
+        (e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev)) != cudaSuccess)
+      return cuda_fail(name, e);
+    g_cc[dev] = major * 10 + minor;
+    g_optin[dev] = optin;
+  }
+  if (g_status[dev] == nullptr) {
+    int* p = nullptr;
+    if ((e = cudaMalloc(&p, 256)) != cudaSuccess) return cuda_fail(name, e);
+    if ((e = cudaMemset(p, 0, 256)) != cudaSuccess) return cuda_fail(name, e);
+    g_status[dev] = p;
+  }
+  out->id = dev;
+  out->cc = g_cc[dev];
+  out->optin = g_optin[dev];
+  out->status = g_status[dev];
+  return PHANTOM_ATTN_OK;
+}
+
+// Device-pointer check: each of q, k, v, o must be device (or managed) memory of device `dev`.
+int check_pointers(const char* name, const void* const* ptrs, int dev) {
+  for (int i = 0; i < 4; ++i) {
+    if (ptrs[i] == nullptr) return fail(PHANTOM_ATTN_ERR_INVALID, "%s: inputs must be CUDA tensors (null pointer)", name);
+    cudaPointerAttributes attr;
+    cudaError_t e = cudaPointerGetAttributes(&attr, ptrs[i]);
+    if (e != cudaSuccess) {
+      cudaGetLastError();
+      return fail(PHANTOM_ATTN_ERR_INVALID, "%s: inputs must be CUDA tensors", name);
+    }
+    if (attr.type != cudaMemoryTypeDevice && attr.type != cudaMemoryTypeManaged)
+      return fail(PHANTOM_ATTN_ERR_INVALID, "%s: inputs must be CUDA tensors", name);
+    if (attr.type == cudaMemoryTypeDevice && attr.device != dev)
+      return fail(PHANTOM_ATTN_ERR_INVALID, "%s: q, k, v must be on the same device (current device %d)", name, dev);
+  }
+  return PHANTOM_ATTN_OK;
+}
+
+int check_common(const char* name, const void* q, const void* k, const void* v, void* o, int BH, int N, int d,
+                 int dtype, Device* dev) {
+  if (BH <= 0 || N <= 0 || d <= 0) return fail(PHANTOM_ATTN_ERR_INVALID, "%s: inputs must be non-empty", name);
+  if (dtype != PHANTOM_ATTN_F32 && dtype != PHANTOM_ATTN_F16 && dtype != PHANTOM_ATTN_BF16)
+    return fail(PHANTOM_ATTN_ERR_INVALID, "%s: unknown dtype code %d", name, dtype);
+  if ((long long)BH > 65535) return fail(PHANTOM_ATTN_ERR_UNSUPPORTED, "%s: batch*heads = %d exceeds 65535", name, BH);
+  int rc = current_device(name, dev);
+  if (rc != PHANTOM_ATTN_OK) return rc;
+  const void* ptrs[4] = {q, k, v, o};
+  return check_pointers(name, ptrs, dev->id);
+}
+
+int run(const char* name, cudaError_t (*launch)(const LaunchArgs&), const void* q, const void* k, const void* v,
+        void* o, int BH, int N, int d, int dtype, int causal, void* stream, const Device& dev) {
+  LaunchArgs a{q, k, v, o, BH, N, d, dtype, causal != 0, static_cast<cudaStream_t>(stream), dev.status};
+  cudaError_t e = launch(a);
+  if (e != cudaSuccess) return cuda_fail(name, e);
+  g_last_error.clear();
+  return PHANTOM_ATTN_OK;
+}
+
+int tc_entry(const char* name, const void* q, const void* k, const void* v, void* o, int BH, int N, int d, int dtype,
+             int causal, void* stream) {
+  Device dev;
+  int rc = check_common(name, q, k, v, o, BH, N, d, dtype, &dev);
+  if (rc != PHANTOM_ATTN_OK) return rc;
+  if (dtype == PHANTOM_ATTN_F32)
+    return fail(PHANTOM_ATTN_ERR_UNSUPPORTED, "%s: float16 or bfloat16 only (tensor cores)", name);
+  if (d != 64 && d != 128)
+    return fail(PHANTOM_ATTN_ERR_UNSUPPORTED, "%s: only head dimension 64 and 128 are compiled (got %d)", name, d);
+  for (const void* p : {q, k, v, static_cast<const void*>(o)})
+    if (reinterpret_cast<uintptr_t>(p) % 16 != 0)
+      return fail(PHANTOM_ATTN_ERR_INVALID, "%s: inputs must be 16-byte aligned", name);
+  if (dev.cc != 100)
+    return fail(PHANTOM_ATTN_ERR_UNSUPPORTED,
+                "%s: the tcgen05 kernel is compiled for sm_100a (B200); this GPU is sm_%d", name, dev.cc);
+  const size_t smem = fused_tc_smem_bytes(d);
+  if (smem > (size_t)dev.optin)
+    return fail(PHANTOM_ATTN_ERR_UNSUPPORTED, "%s: needs %zu bytes of shared memory, GPU allows %d", name, smem,
+                dev.optin);
+  return run(name, launch_fused_tc_sm100, q, k, v, o, BH, N, d, dtype, causal, stream, dev);
+}
+
+int simt_entry(const char* name, const void* q, const void* k, const void* v, void* o, int BH, int N, int d,
+               int dtype, int causal, void* stream) {
+  Device dev;
+  int rc = check_common(name, q, k, v, o, BH, N, d, dtype, &dev);
+  if (rc != PHANTOM_ATTN_OK) return rc;
+  if (d > 256)
+    return fail(PHANTOM_ATTN_ERR_UNSUPPORTED, "%s: head dimension up to 256 is compiled (got %d)", name, d);
+  const size_t smem = fused_simt_smem_bytes(d);
+  if (smem > (size_t)dev.optin)
+    return fail(PHANTOM_ATTN_ERR_UNSUPPORTED, "%s: needs %zu bytes of shared memory, GPU allows %d", name, smem,
+                dev.optin);
+  return run(name, launch_fused_simt, q, k, v, o, BH, N, d, dtype, causal, stream, dev);
+}
+
+}  // namespace
+
+void note_launch() { ++g_launches; }
+
+}  // namespace phantom
+
+using namespace phantom;
+
+extern "C" {
+
+int phantom_attn_version(void) { return 10000; }
+
+const char* phantom_attn_last_error(void) { return g_last_error.c_str(); }
+
+int phantom_attn_fused_tc(const void* q, const void* k, const void* v, void* o, int BH, int N, int head_dim,
+                          int dtype, int causal, void* stream) {
+  return tc_entry("fused_tc", q, k, v, o, BH, N, head_dim, dtype, causal, stream);
+}
+
+int phantom_attn_fused_tuned(const void* q, const void* k, const void* v, void* o, int BH, int N, int head_dim,
+                             int dtype, int causal, int double_buffer, int br, int bc, void* stream) {
+  (void)double_buffer;
+  const bool compiled = (br == 64 || br == 128) && (bc == 32 || bc == 64);
+  if (!compiled)
+    return fail(PHANTOM_ATTN_ERR_UNSUPPORTED,
+                "fused_tuned: (br, bc) = (%d, %d) not compiled; available: (64,32) (64,64) (128,32) (128,64)", br, bc);
+  return tc_entry("fused_tuned", q, k, v, o, BH, N, head_dim, dtype, causal, stream);
+}
+
+int phantom_attn_fused(const void* q, const void* k, const void* v, void* o, int BH, int N, int head_dim, int dtype,
+                       int causal, void* stream) {
+  return simt_entry("fused", q, k, v, o, BH, N, head_dim, dtype, causal, stream);
+}
+
+int phantom_attn_naive(const void* q, const void* k, const void* v, void* o, int BH, int N, int head_dim, int dtype,
+                       int causal, void* stream) {
+  return simt_entry("naive", q, k, v, o, BH, N, head_dim, dtype, causal, stream);
+}
+
+int phantom_attn_tiled(const void* q, const void* k, const void* v, void* o, int BH, int N, int head_dim, int dtype,
+                       int causal, void* stream) {
+  return simt_entry("tiled", q, k, v, o, BH, N, head_dim, dtype, causal, stream);
+}
+
+int phantom_attn_device_status(int* status) {
+  if (status == nullptr) return fail(PHANTOM_ATTN_ERR_INVALID, "device_status: null output pointer");
+  *status = 0;
+  Device dev;
+  int rc = current_device("device_status", &dev);
+  if (rc != PHANTOM_ATTN_OK) return rc;
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return cuda_fail("device_status", e);
+  int v = 0;
+  if ((e = cudaMemcpy(&v, dev.status, sizeof(int), cudaMemcpyDeviceToHost)) != cudaSuccess)
+    return cuda_fail("device_status", e);
+  if (v != 0 && (e = cudaMemset(dev.status, 0, sizeof(int))) != cudaSuccess) return cuda_fail("device_status", e);
+  *status = v;
+  g_last_error.clear();
+  return v == 0 ? PHANTOM_ATTN_OK : fail(PHANTOM_ATTN_ERR_DEVICE, "device status 0x%x: a bounded wait expired", v);
+}
+
+long long phantom_attn_launch_count(int reset) {
+  const long long n = g_launches;
+  if (reset) g_launches = 0;
+  return n;
+}
+
+}  // extern "C"

@@ -1,0 +1,33 @@
+#pragma once
+// Internal launcher interface between the C ABI (capi.cu) and the kernels. Torch-free.
+#include <cuda_runtime.h>
+
+namespace phantom {
+
+struct LaunchArgs {
+  const void* q;
+  const void* k;
+  const void* v;
+  void* o;
+  int BH;
+  int N;
+  int d;
+  int dtype;   // PHANTOM_ATTN_F32 / F16 / BF16
+  bool causal;
+  cudaStream_t stream;
+  int* status;  // device status word (bounded-wait expiry bits), may be null for kernels without waits
+};
+
+// Tensor-core kernel (sm_100a tcgen05). d in {64, 128}, dtype F16/BF16.
+cudaError_t launch_fused_tc_sm100(const LaunchArgs& a);
+// Dynamic shared memory the tensor-core kernel needs for head dim d.
+size_t fused_tc_smem_bytes(int d);
+
+// CUDA-core fp32-arithmetic kernel. Any d in [1, 256], dtype F32/F16/BF16.
+cudaError_t launch_fused_simt(const LaunchArgs& a);
+size_t fused_simt_smem_bytes(int d);
+
+// Number of kernel launches the library has made on this thread (benchmark accounting).
+void note_launch();
+
+}  // namespace phantom
