@@ -101,6 +101,16 @@ int phantom_attn_device_status(int* status);
  */
 long long phantom_attn_launch_count(int reset);
 
+/*
+ * Benchmark support (no counterpart in the reference). While enabled on the calling thread, every
+ * launch of the tensor-core attention kernel is bracketed by a CUDA event pair recorded on its stream
+ * (the bf16 V staging pass is outside the pair). enable = 1 also discards earlier records.
+ * phantom_attn_kernel_timing_read() waits for the recorded events and returns the summed kernel time
+ * in milliseconds and the number of bracketed launches.
+ */
+int phantom_attn_kernel_timing(int enable);
+int phantom_attn_kernel_timing_read(double* total_ms, long long* launches);
+
 #ifdef __cplusplus
 }
 #endif

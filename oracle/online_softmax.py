@@ -64,7 +64,8 @@ def sampled_rows_naive(q: np.ndarray, k: np.ndarray, v: np.ndarray, rows: np.nda
 
 
 def attention_online(q: np.ndarray, k: np.ndarray, v: np.ndarray, causal: bool = False, br: int = 64,
-                     bc: int = 32, p_dtype: str | None = None, p_fp16: bool = False) -> np.ndarray:
+                     bc: int = 32, p_dtype: str | None = None, p_fp16: bool = False,
+                     row_offset: int = 0) -> np.ndarray:
     """Tile-by-tile online softmax in float32, the way the fused kernels compute it
     (online_softmax_ref.py:27-63).
 
@@ -72,25 +73,30 @@ def attention_online(q: np.ndarray, k: np.ndarray, v: np.ndarray, causal: bool =
     per row a running max m and running sum l; alpha = exp2(m_old - m_new) rescales l and O; the output
     is O / l. p_dtype ("float16" / "bfloat16") rounds P before the P @ V product while l sums the
     unrounded values - the model of a tensor-core P.V (p_fp16=True is the reference's name for
-    p_dtype="float16")."""
+    p_dtype="float16").
+
+    Extension for row-sampled checks and baselines: q may hold fewer rows than k / v (a contiguous slice
+    of the queries starting at global row `row_offset`); with equal lengths and row_offset = 0 this is
+    exactly the reference function."""
     if p_fp16:
         p_dtype = "float16"
     q32, k32, v32 = (np.asarray(x, dtype=np.float32) for x in (q, k, v))
-    *lead, n, d = q32.shape
+    *lead, n_q, d = q32.shape
+    n_k = k32.shape[-2]
     out = np.empty_like(q32)
     scale_log2 = np.float32(LOG2E / np.sqrt(d))
     neg_inf = np.float32(-np.inf)
 
-    for r0 in range(0, n, br):
-        r1 = min(r0 + br, n)
+    for r0 in range(0, n_q, br):
+        r1 = min(r0 + br, n_q)
         qs = q32[..., r0:r1, :] * scale_log2
-        rows = np.arange(r0, r1)
+        rows = np.arange(r0, r1) + row_offset
         m = np.full((*lead, r1 - r0), neg_inf, dtype=np.float32)
         l = np.zeros((*lead, r1 - r0), dtype=np.float32)
         acc = np.zeros((*lead, r1 - r0, d), dtype=np.float32)
-        stop = min(n, r1) if causal else n
+        stop = min(n_k, row_offset + r1) if causal else n_k
         for c0 in range(0, stop, bc):
-            c1 = min(c0 + bc, n)
+            c1 = min(c0 + bc, n_k)
             s = np.matmul(qs, np.swapaxes(k32[..., c0:c1, :], -1, -2))
             if causal:
                 s = np.where(np.arange(c0, c1)[None, :] > rows[:, None], neg_inf, s)

@@ -4,9 +4,12 @@
 //
 // Algorithm (same arithmetic contract as the reference's v4 kernel, csrc/kernels/fused_tc.cuh:45-179,
 // and its NumPy model cuda_attn/online_softmax_ref.py:27-63 with p_fp16=True): scores in fp32, a
-// running row max m and row sum l in fp32, P = exp2(S*log2e/sqrt(d) - m) rounded to the input dtype
-// for the P.V product while l sums the unrounded fp32 values, O accumulated in fp32 and divided by l
-// once at the end.
+// running row max m and row sum l in fp32, P = exp2(S*log2e/sqrt(d) - m) rounded to fp16 for the P.V
+// product while l sums the unrounded fp32 values, O accumulated in fp32 and divided by l at the end.
+// bf16 inputs: Q K^T runs in bf16; V is first staged as fp16 by stage_v_f16 (exact for every bf16
+// value inside the fp16 range) so that P.V also runs with fp16 P - rounding P to bf16 instead would
+// alone give a relative-L2 error of ~2.4e-3, above the 1e-3 parity bound. A head whose V holds a
+// finite value beyond the fp16 range falls back to bf16 P and the original bf16 V for that head.
 //
 // B200 mapping (not a translation of the WMMA kernel):
 //   * One CTA owns two 128-row Q tiles (A, B) of one (batch, head) and streams K/V tiles of 128 keys.
@@ -78,11 +81,60 @@ __device__ __forceinline__ void ld128(uint32_t taddr, float (&s)[128]) {
   for (int i = 0; i < 64; ++i) s[64 + i] = __uint_as_float(r[i]);
 }
 
+// V staging for bf16 inputs: Vh = fp16(V), per (head, chunk) flag = 1 if a finite V value of the
+// chunk lies outside the fp16 range (it would become inf). Grid (kVChunks, BH), 16-byte vectors.
+constexpr int kVChunks = 32;
+
+__global__ void __launch_bounds__(256)
+stage_v_f16(const uint4* __restrict__ V, uint4* __restrict__ Vh, int* __restrict__ flags, long long vec_per_head) {
+  const int bh = blockIdx.y;
+  const long long per_chunk = (vec_per_head + kVChunks - 1) / kVChunks;
+  const long long b = (long long)blockIdx.x * per_chunk;
+  const long long e = min(vec_per_head, b + per_chunk);
+  const uint4* src = V + (long long)bh * vec_per_head;
+  uint4* dst = Vh + (long long)bh * vec_per_head;
+  int ovf = 0;
+  for (long long i = b + threadIdx.x; i < e; i += blockDim.x) {
+    const uint4 w = src[i];
+    uint32_t in[4] = {w.x, w.y, w.z, w.w}, out[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float lo = __uint_as_float(in[j] << 16), hi = __uint_as_float(in[j] & 0xFFFF0000u);
+      ovf |= (fabsf(lo) >= 65520.f && fabsf(lo) != CUDART_INF_F) | (fabsf(hi) >= 65520.f && fabsf(hi) != CUDART_INF_F);
+      out[j] = pack2<false>(lo, hi);
+    }
+    dst[i] = make_uint4(out[0], out[1], out[2], out[3]);
+  }
+  ovf = __syncthreads_or(ovf);
+  if (threadIdx.x == 0) flags[bh * kVChunks + blockIdx.x] = ovf;
+}
+
+// Softmax of one S row already in registers: P = exp2(s*scale - m_sub) packed as 16-bit pairs into
+// two 32-word halves; returns the fp32 row sum of the unrounded values.
+template <bool P_BF16>
+__device__ __forceinline__ float softmax_pack(const float (&s)[128], float scale_log2, float m_sub,
+                                              uint32_t (&p_lo)[32], uint32_t (&p_hi)[32]) {
+  float rowsum = 0.f;
+#pragma unroll
+  for (int c = 0; c < 32; ++c) {
+    const float p0 = ex2(fmaf(s[2 * c], scale_log2, -m_sub));
+    const float p1 = ex2(fmaf(s[2 * c + 1], scale_log2, -m_sub));
+    const float p2 = ex2(fmaf(s[64 + 2 * c], scale_log2, -m_sub));
+    const float p3 = ex2(fmaf(s[64 + 2 * c + 1], scale_log2, -m_sub));
+    rowsum += (p0 + p1) + (p2 + p3);
+    p_lo[c] = pack2<P_BF16>(p0, p1);
+    p_hi[c] = pack2<P_BF16>(p2, p3);
+  }
+  return rowsum;
+}
+
+// BF16: input/output dtype. vflags (bf16 only): per-(head, chunk) fp16-overflow flags of V.
 template <int D, bool BF16>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
 attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-            const __grid_constant__ CUtensorMap tmV, uint16_t* __restrict__ O, int N, float scale_log2,
-            int causal, int* __restrict__ status) {
+            const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmVh,
+            const int* __restrict__ vflags, uint16_t* __restrict__ O, int N, float scale_log2, int causal,
+            int* __restrict__ status) {
   using C = Cfg<D>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -97,6 +149,7 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
   const uint32_t drain_bar = bar0 + 8u * (7 + 2 * C::STAGES);
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 4);
+  int* pv_bf16_flag = reinterpret_cast<int*>(smem + C::OFF_MISC + 8);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int bh = blockIdx.y;
@@ -127,10 +180,18 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
     tmem_alloc(smem_u32(tmem_holder), C::TMEM_COLS);
     tmem_relinquish();
   }
+  if (warp == MMA_WARP + 2) {
+    // P.V precision of this head: fp16 unless a V value of the head overflows fp16 (bf16 inputs).
+    int ovf = 0;
+    if (BF16) ovf = vflags[bh * kVChunks + lane] != 0;
+    ovf = __any_sync(0xffffffffu, ovf);
+    if (lane == 0) *pv_bf16_flag = ovf;
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
+  const bool pv_bf16 = BF16 && *pv_bf16_flag != 0;  // CTA-uniform
 
   if (warp == TMA_WARP || warp >= MMA_WARP + 2) {
     setmaxnreg_dec<kRegsProducer>();
@@ -138,6 +199,8 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
       tma_prefetch_desc(&tmQ);
       tma_prefetch_desc(&tmK);
       tma_prefetch_desc(&tmV);
+      const CUtensorMap* tm_v = (BF16 && !pv_bf16) ? &tmVh : &tmV;
+      tma_prefetch_desc(tm_v);
       const int nq = has_b ? 2 : 1;
       mbar_arrive_expect_tx(q_full(), nq * C::TILE_BYTES);
       for (int g = 0; g < nq; ++g)
@@ -149,7 +212,7 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
         const int s = t % C::STAGES, r = t / C::STAGES;
         if (r > 0 && !mbar_wait(kv_empty(s), (r - 1) & 1, abort_flag, status, kErrTmaWait)) break;
         mbar_arrive_expect_tx(kv_full(s), C::TILE_BYTES);
-        const CUtensorMap* m = (t & 1) ? &tmV : &tmK;
+        const CUtensorMap* m = (t & 1) ? tm_v : &tmK;
         const int j = t >> 1;
         for (int c = 0; c < C::KBLK; ++c)
           tma_load_3d(sbase + C::OFF_KV + s * C::TILE_BYTES + c * C::SUB_BYTES, m, kv_full(s), c * 64, j * BN, bh);
@@ -164,7 +227,7 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
     setmaxnreg_dec<kRegsProducer>();
     if (lane == 0) {
       constexpr uint32_t idesc_qk = idesc_f16(BF16, BM, BN, false);
-      constexpr uint32_t idesc_pv = idesc_f16(BF16, BM, D, true);
+      const uint32_t idesc_pv = idesc_f16(pv_bf16, BM, D, true);
       auto issue_qk = [&](int g, int stage) {
         const uint32_t a0 = sbase + C::OFF_Q + g * C::TILE_BYTES;
         const uint32_t b0 = sbase + C::OFF_KV + stage * C::TILE_BYTES;
@@ -284,19 +347,11 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
           }
         }
         const float m_sub = m_used == -CUDART_INF_F ? 0.f : m_used;
-        float rowsum = 0.f;
         uint32_t p_lo[32], p_hi[32];
-#pragma unroll
-        for (int c = 0; c < 32; ++c) {
-          const float p0 = ex2(fmaf(s[2 * c], scale_log2, -m_sub));
-          const float p1 = ex2(fmaf(s[2 * c + 1], scale_log2, -m_sub));
-          const float p2 = ex2(fmaf(s[64 + 2 * c], scale_log2, -m_sub));
-          const float p3 = ex2(fmaf(s[64 + 2 * c + 1], scale_log2, -m_sub));
-          rowsum += (p0 + p1) + (p2 + p3);
-          p_lo[c] = pack2<BF16>(p0, p1);
-          p_hi[c] = pack2<BF16>(p2, p3);
-        }
-        l += rowsum;
+        if (pv_bf16)
+          l += softmax_pack<true>(s, scale_log2, m_sub, p_lo, p_hi);
+        else
+          l += softmax_pack<false>(s, scale_log2, m_sub, p_lo, p_hi);
         tmem_st32(t_s, p_lo);
         tmem_st32(t_s + 32, p_hi);
         tmem_wait_st();
@@ -374,14 +429,43 @@ bool make_map(CUtensorMap* m, const void* base, int BH, int N, int d, bool bf16)
   return r == CUDA_SUCCESS;
 }
 
+// Stream-ordered scratch for the bf16 V staging: one memory pool per device, owned by the library,
+// that keeps freed blocks cached (release threshold = max) so repeated calls do not go back to the
+// driver. Allocation and free are ordered on the caller's stream, so concurrent calls on different
+// streams each get their own block.
+constexpr int kMaxDevices = 64;
+cudaMemPool_t g_pool[kMaxDevices] = {};
+std::mutex g_pool_mu;
+
+cudaError_t device_pool(int dev, cudaMemPool_t* out) {
+  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lock(g_pool_mu);
+  if (g_pool[dev] == nullptr) {
+    cudaMemPoolProps props = {};
+    props.allocType = cudaMemAllocationTypePinned;
+    props.location.type = cudaMemLocationTypeDevice;
+    props.location.id = dev;
+    cudaMemPool_t pool;
+    cudaError_t e = cudaMemPoolCreate(&pool, &props);
+    if (e != cudaSuccess) return e;
+    uint64_t keep = ~0ull;
+    e = cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep);
+    if (e != cudaSuccess) return e;
+    g_pool[dev] = pool;
+  }
+  *out = g_pool[dev];
+  return cudaSuccess;
+}
+
 template <int D, bool BF16>
-cudaError_t launch_t(const LaunchArgs& a, const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv) {
+cudaError_t launch_t(const LaunchArgs& a, const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
+                     const CUtensorMap& mvh, const int* vflags) {
   auto kern = tc::attn_fwd_tc<D, BF16>;
   constexpr int smem = tc::Cfg<D>::SMEM_BYTES;
-  static bool attr_set[64] = {};  // per device
+  static bool attr_set[kMaxDevices] = {};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev < 64 && !attr_set[dev]) {
+  if (dev < kMaxDevices && !attr_set[dev]) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     attr_set[dev] = true;
@@ -389,10 +473,39 @@ cudaError_t launch_t(const LaunchArgs& a, const CUtensorMap& mq, const CUtensorM
   const int n_qtiles = (a.N + tc::BM - 1) / tc::BM;
   const dim3 grid((n_qtiles + 1) / 2, a.BH);
   const float scale_log2 = 1.4426950408889634f / sqrtf((float)D);
-  kern<<<grid, tc::NUM_THREADS, smem, a.stream>>>(mq, mk, mv, static_cast<uint16_t*>(a.o), a.N, scale_log2,
-                                                   a.causal ? 1 : 0, a.status);
+  timing_begin(a.stream);
+  kern<<<grid, tc::NUM_THREADS, smem, a.stream>>>(mq, mk, mv, mvh, vflags, static_cast<uint16_t*>(a.o), a.N,
+                                                   scale_log2, a.causal ? 1 : 0, a.status);
+  timing_end(a.stream);
   note_launch();
   return cudaGetLastError();
+}
+
+template <int D>
+cudaError_t launch_d(const LaunchArgs& a, const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv) {
+  if (a.dtype != PHANTOM_ATTN_BF16) return launch_t<D, false>(a, mq, mk, mv, mv, nullptr);
+  // bf16: stage V as fp16 in stream-ordered scratch [Vh | flags], run, release.
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  cudaMemPool_t pool;
+  if ((e = device_pool(dev, &pool)) != cudaSuccess) return e;
+  const size_t vh_bytes = (size_t)a.BH * a.N * D * 2;
+  const size_t flag_bytes = (size_t)a.BH * tc::kVChunks * sizeof(int);
+  void* scratch = nullptr;
+  if ((e = cudaMallocFromPoolAsync(&scratch, vh_bytes + flag_bytes, pool, a.stream)) != cudaSuccess) return e;
+  void* vh = scratch;
+  int* flags = reinterpret_cast<int*>(static_cast<char*>(scratch) + vh_bytes);
+  const long long vec_per_head = (long long)a.N * D / 8;
+  tc::stage_v_f16<<<dim3(tc::kVChunks, a.BH), 256, 0, a.stream>>>(
+      static_cast<const uint4*>(a.v), static_cast<uint4*>(vh), flags, vec_per_head);
+  note_launch();
+  e = cudaGetLastError();
+  CUtensorMap mvh;
+  if (e == cudaSuccess && !make_map(&mvh, vh, a.BH, a.N, D, false)) e = cudaErrorInvalidValue;
+  if (e == cudaSuccess) e = launch_t<D, true>(a, mq, mk, mv, mvh, flags);
+  const cudaError_t ef = cudaFreeAsync(scratch, a.stream);
+  return e != cudaSuccess ? e : ef;
 }
 
 }  // namespace
@@ -405,8 +518,7 @@ cudaError_t launch_fused_tc_sm100(const LaunchArgs& a) {
   if (!make_map(&mq, a.q, a.BH, a.N, a.d, bf16) || !make_map(&mk, a.k, a.BH, a.N, a.d, bf16) ||
       !make_map(&mv, a.v, a.BH, a.N, a.d, bf16))
     return cudaErrorInvalidValue;
-  if (a.d == 64) return bf16 ? launch_t<64, true>(a, mq, mk, mv) : launch_t<64, false>(a, mq, mk, mv);
-  return bf16 ? launch_t<128, true>(a, mq, mk, mv) : launch_t<128, false>(a, mq, mk, mv);
+  return a.d == 64 ? launch_d<64>(a, mq, mk, mv) : launch_d<128>(a, mq, mk, mv);
 }
 
 }  // namespace phantom

@@ -7,6 +7,8 @@
 #include <cstdio>
 #include <mutex>
 #include <string>
+#include <utility>
+#include <vector>
 
 #include "launchers.h"
 #include "../../include/phantom_attn.h"
@@ -16,6 +18,15 @@ namespace {
 
 thread_local std::string g_last_error;
 thread_local long long g_launches = 0;
+
+// Benchmark event brackets: a reusable pool of event pairs per thread.
+struct Timing {
+  bool enabled = false;
+  std::vector<std::pair<cudaEvent_t, cudaEvent_t>> pairs;
+  size_t used = 0;
+  int device = -1;
+};
+thread_local Timing g_timing;
 
 int fail(int code, const char* fmt, ...) {
   char buf[512];
@@ -152,6 +163,28 @@ int simt_entry(const char* name, const void* q, const void* k, const void* v, vo
 
 void note_launch() { ++g_launches; }
 
+void timing_begin(cudaStream_t s) {
+  Timing& t = g_timing;
+  if (!t.enabled) return;
+  if (t.used == t.pairs.size()) {
+    std::pair<cudaEvent_t, cudaEvent_t> p;
+    if (cudaEventCreate(&p.first) != cudaSuccess) return;
+    if (cudaEventCreate(&p.second) != cudaSuccess) {
+      cudaEventDestroy(p.first);
+      return;
+    }
+    t.pairs.push_back(p);
+  }
+  cudaEventRecord(t.pairs[t.used].first, s);
+}
+
+void timing_end(cudaStream_t s) {
+  Timing& t = g_timing;
+  if (!t.enabled || t.used >= t.pairs.size()) return;
+  cudaEventRecord(t.pairs[t.used].second, s);
+  ++t.used;
+}
+
 }  // namespace phantom
 
 using namespace phantom;
@@ -207,6 +240,28 @@ int phantom_attn_device_status(int* status) {
   *status = v;
   g_last_error.clear();
   return v == 0 ? PHANTOM_ATTN_OK : fail(PHANTOM_ATTN_ERR_DEVICE, "device status 0x%x: a bounded wait expired", v);
+}
+
+int phantom_attn_kernel_timing(int enable) {
+  g_timing.enabled = enable != 0;
+  g_timing.used = 0;
+  return PHANTOM_ATTN_OK;
+}
+
+int phantom_attn_kernel_timing_read(double* total_ms, long long* launches) {
+  if (!total_ms || !launches) return fail(PHANTOM_ATTN_ERR_INVALID, "kernel_timing_read: null output pointer");
+  double sum = 0.0;
+  for (size_t i = 0; i < g_timing.used; ++i) {
+    cudaError_t e = cudaEventSynchronize(g_timing.pairs[i].second);
+    if (e != cudaSuccess) return cuda_fail("kernel_timing_read", e);
+    float ms = 0.f;
+    if ((e = cudaEventElapsedTime(&ms, g_timing.pairs[i].first, g_timing.pairs[i].second)) != cudaSuccess)
+      return cuda_fail("kernel_timing_read", e);
+    sum += ms;
+  }
+  *total_ms = sum;
+  *launches = (long long)g_timing.used;
+  return PHANTOM_ATTN_OK;
 }
 
 long long phantom_attn_launch_count(int reset) {

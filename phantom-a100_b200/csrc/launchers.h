@@ -30,4 +30,8 @@ size_t fused_simt_smem_bytes(int d);
 // Number of kernel launches the library has made on this thread (benchmark accounting).
 void note_launch();
 
+// Benchmark event brackets around the main attention kernel (no-ops unless enabled on this thread).
+void timing_begin(cudaStream_t s);
+void timing_end(cudaStream_t s);
+
 }  // namespace phantom

@@ -30,6 +30,8 @@ SIGNATURES = {
     "phantom_attn_tiled": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _I, _P]),
     "phantom_attn_device_status": (_I, [ctypes.POINTER(ctypes.c_int)]),
     "phantom_attn_launch_count": (ctypes.c_longlong, [_I]),
+    "phantom_attn_kernel_timing": (_I, [_I]),
+    "phantom_attn_kernel_timing_read": (_I, [ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_longlong)]),
 }
 
 
@@ -114,3 +116,12 @@ class CAPI:
 
     def launch_count(self, reset: bool = False) -> int:
         return int(self.lib.phantom_attn_launch_count(int(reset)))
+
+    def kernel_timing(self, enable: bool) -> None:
+        self._check(self.lib.phantom_attn_kernel_timing(int(enable)))
+
+    def kernel_timing_read(self) -> tuple[float, int]:
+        """(summed milliseconds, launches) of the tensor-core kernel since timing was enabled."""
+        ms, n = ctypes.c_double(0.0), ctypes.c_longlong(0)
+        self._check(self.lib.phantom_attn_kernel_timing_read(ctypes.byref(ms), ctypes.byref(n)))
+        return ms.value, n.value

@@ -1,0 +1,165 @@
+"""GPU parity: the sm_100a kernels, called through the C ABI (libphantom_attn.so via ctypes), against the
+CPU oracle on identical seeded inputs.
+
+Criteria (conftest.py): fp32 max-abs 1e-4; fp16/bf16 relative-L2 1e-3 and max-abs 2e-3 beyond one
+output ulp, against the float64 oracle rounded to the output dtype. Full-size BASELINE configs are
+checked on sampled query rows (rows are independent, so the sampled oracle is exact) plus properties
+that hold at any size: every row written and finite, each output inside the convex hull of V's
+columns, bit-identical reruns.
+"""
+import numpy as np
+import pytest
+import torch
+
+from conftest import assert_parity, make_qkv, torch_dtype_name
+from oracle import attention_naive, sampled_rows_naive
+
+pytestmark = pytest.mark.gpu
+
+SMALL_N = [1, 15, 64, 65, 127, 128, 129, 255, 256, 257, 511, 1000]
+
+
+def np64(t):
+    return t.float().cpu().numpy().astype(np.float64)
+
+
+def run_capi(capi, fn_name, q, k, v, causal=False, **kw):
+    o = torch.full_like(q, float("nan"))  # canary: every element must be written
+    getattr(capi, fn_name)(q, k, v, o, causal=causal, **kw)
+    torch.cuda.synchronize()
+    return o
+
+
+@pytest.fixture(autouse=True)
+def _status_clean(cuda_ok, capi):
+    yield
+    assert capi.device_status() == 0, "a bounded device wait expired"
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("d", [64, 128])
+@pytest.mark.parametrize("n", SMALL_N)
+@pytest.mark.parametrize("causal", [False, True])
+def test_fused_tc_matches_oracle(capi, dtype, d, n, causal):
+    q, k, v = make_qkv(1, 2, n, d, dtype, seed=n)
+    o = run_capi(capi, "fused_tc", q, k, v, causal)
+    ref = attention_naive(np64(q), np64(k), np64(v), causal)
+    assert_parity(np64(o), ref, torch_dtype_name(dtype), f"fused_tc {dtype} d={d} n={n} causal={causal}")
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("d", [32, 64, 80, 128, 256])
+@pytest.mark.parametrize("n", [1, 63, 65, 200])
+@pytest.mark.parametrize("fn", ["fused", "naive", "tiled"])
+def test_cuda_core_kernel_matches_oracle(capi, dtype, d, n, fn):
+    causal = n == 63
+    q, k, v = make_qkv(1, 2, n, d, dtype, seed=d + n)
+    o = run_capi(capi, fn, q, k, v, causal)
+    ref = attention_naive(np64(q), np64(k), np64(v), causal)
+    assert_parity(np64(o), ref, torch_dtype_name(dtype), f"{fn} {dtype} d={d} n={n}")
+
+
+@pytest.mark.parametrize("br,bc", [(64, 32), (64, 64), (128, 32), (128, 64)])
+@pytest.mark.parametrize("double_buffer", [False, True])
+def test_fused_tuned_tiles_run_the_tensor_core_kernel(capi, br, bc, double_buffer):
+    q, k, v = make_qkv(2, 3, 333, 64, torch.float16)
+    o = run_capi(capi, "fused_tuned", q, k, v, True, double_buffer=double_buffer, br=br, bc=bc)
+    o_tc = run_capi(capi, "fused_tc", q, k, v, True)
+    assert torch.equal(o, o_tc)
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("scale", [10.0, 30.0])
+def test_large_scores_do_not_overflow(capi, dtype, scale):
+    q, k, v = make_qkv(1, 2, 256, 64, dtype)
+    q, k = (q.float() * scale).to(dtype), (k.float() * scale).to(dtype)
+    o = run_capi(capi, "fused_tc", q, k, v)
+    assert torch.isfinite(o).all()
+    ref = attention_naive(np64(q), np64(k), np64(v))
+    assert np.abs(np64(o) - ref).max() < 1e-2 + 2.0 ** -7  # reference tolerance at this scale (+ bf16 ulp)
+
+
+def test_bf16_head_beyond_fp16_range_falls_back_to_bf16_p(capi):
+    """A bf16 V value outside the fp16 range makes that head compute P.V in bf16 (finite, looser bound);
+    the other heads keep fp16 P and the tight bound."""
+    q, k, v = make_qkv(1, 2, 300, 128, torch.bfloat16, seed=5)
+    v[0, 1, 17, 3] = 1.0e6
+    o = run_capi(capi, "fused_tc", q, k, v)
+    ref = attention_naive(np64(q), np64(k), np64(v))
+    assert torch.isfinite(o).all()
+    assert_parity(np64(o)[:, :1], ref[:, :1], "bfloat16", "head 0 (fp16 P)")
+    rel = np.linalg.norm(np64(o)[:, 1] - ref[:, 1]) / np.linalg.norm(ref[:, 1])
+    assert rel < 5e-3, rel
+
+
+def test_non_default_stream(capi):
+    q, k, v = make_qkv(1, 4, 777, 128, torch.bfloat16, seed=3)
+    s = torch.cuda.Stream()
+    o = torch.empty_like(q)
+    with torch.cuda.stream(s):
+        capi.fused_tc(q, k, v, o, stream=s)
+    s.synchronize()
+    ref = attention_naive(np64(q), np64(k), np64(v))
+    assert_parity(np64(o), ref, "bfloat16", "non-default stream")
+
+
+def test_reruns_are_bit_identical(capi):
+    q, k, v = make_qkv(2, 4, 1500, 128, torch.bfloat16, seed=8)
+    a = run_capi(capi, "fused_tc", q, k, v, True)
+    b = run_capi(capi, "fused_tc", q, k, v, True)
+    assert torch.equal(a, b)
+
+
+# ---------------------------------------------------------------- BASELINE configs at full size
+def check_full_size(capi, q, k, v, causal, dtype_name, heads, n_rows=96, seed=0):
+    o = run_capi(capi, "fused_tc", q, k, v, causal)
+    B, H, N, d = q.shape
+    qf, kf, vf, of = (x.reshape(B * H, N, d) for x in (q, k, v, o))
+    assert torch.isfinite(of).all(), "unwritten or non-finite output"
+    # convex hull: every output element lies within [min_j V[j, c], max_j V[j, c]] of its head
+    vmin = vf.float().amin(dim=1, keepdim=True)
+    vmax = vf.float().amax(dim=1, keepdim=True)
+    slack = 2e-2 * (vmax - vmin).abs() + 1e-3
+    assert bool(((of.float() >= vmin - slack) & (of.float() <= vmax + slack)).all()), "output outside hull of V"
+    rng = np.random.default_rng(seed)
+    for h in heads:
+        rows = np.unique(np.concatenate([[0, N - 1], rng.choice(N, size=min(N, n_rows), replace=False)]))
+        ref = sampled_rows_naive(np64(qf[h]), np64(kf[h]), np64(vf[h]), rows, causal)
+        assert_parity(np64(of[h])[rows], ref, dtype_name, f"head {h} sampled rows")
+    return o
+
+
+def test_config2_full_size(capi):
+    from cuda_attn.workloads import CONFIGS, make_inputs
+    cfg = CONFIGS["config2"]
+    q, k, v = make_inputs(cfg)
+    check_full_size(capi, q, k, v, cfg.causal, "float16", heads=[0, 77, 127])
+
+
+def test_config3_full_size(capi):
+    from cuda_attn.workloads import CONFIGS, make_inputs
+    cfg = CONFIGS["config3"]
+    q, k, v = make_inputs(cfg)
+    check_full_size(capi, q, k, v, cfg.causal, "bfloat16", heads=[0, 64, 127])
+
+
+def test_config4_full_size_with_outliers(capi):
+    from cuda_attn.workloads import CONFIGS, make_inputs
+    cfg = CONFIGS["config4"]
+    q, k, v = make_inputs(cfg)
+    check_full_size(capi, q, k, v, cfg.causal, "bfloat16", heads=[0, 31], n_rows=64)
+
+
+@pytest.mark.parametrize("n", [128, 256, 512, 1024, 2048, 4096, 8192])
+@pytest.mark.parametrize("d", [64, 128])
+def test_config5_sweep(capi, n, d):
+    from cuda_attn.workloads import make_inputs, sweep_config
+    cfg = sweep_config(n, d)
+    q, k, v = make_inputs(cfg)
+    check_full_size(capi, q, k, v, cfg.causal, "float16", heads=[0, 63], n_rows=48)
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_causal_full_size(capi, dtype):
+    q, k, v = make_qkv(1, 4, 4096, 128, dtype, seed=21)
+    check_full_size(capi, q, k, v, True, torch_dtype_name(dtype), heads=[0, 3], n_rows=64)
