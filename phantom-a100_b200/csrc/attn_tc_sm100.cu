@@ -45,10 +45,10 @@ constexpr int MMA_WARP = 8;
 constexpr int TMA_WARP = 9;          // warps 10-11 complete the producer warpgroup and idle
 constexpr int NUM_THREADS = 384;
 // Register split (setmaxnreg): the kernel launches at 168 registers/thread (384 threads, 1 CTA/SM).
-// The producer warpgroup drops to 40 and the two softmax warpgroups rise to 232:
-// 128*(168-40) = 2*128*(232-168), so the increase is exactly covered by the release.
-constexpr int kRegsProducer = 40;
-constexpr int kRegsSoftmax = 232;
+// The producer warpgroup drops to 72 and the two softmax warpgroups rise to 216:
+// 128*(168-72) = 2*128*(216-168), so the increase is exactly covered by the release.
+constexpr int kRegsProducer = 72;
+constexpr int kRegsSoftmax = 216;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale O only when the max grows by > 2^8
 
 // Status-word bits (which wait expired).
@@ -72,13 +72,26 @@ struct Cfg {
 };
 
 __device__ __forceinline__ void ld128(uint32_t taddr, float (&s)[128]) {
-  uint32_t r[64];
-  tmem_ld64_wait(taddr, r);
+  uint32_t r[128];
+  tmem_ld128_wait(taddr, r);
 #pragma unroll
-  for (int i = 0; i < 64; ++i) s[i] = __uint_as_float(r[i]);
-  tmem_ld64_wait(taddr + 64, r);
+  for (int i = 0; i < 128; ++i) s[i] = __uint_as_float(r[i]);
+}
+
+// Maximum of 128 values: a 5-level tree of 3-input maxima (64 instructions, short dependency chain).
+__device__ __forceinline__ float row_max128(const float (&s)[128]) {
+  float x[43];
 #pragma unroll
-  for (int i = 0; i < 64; ++i) s[64 + i] = __uint_as_float(r[i]);
+  for (int i = 0; i < 42; ++i) x[i] = max3(s[3 * i], s[3 * i + 1], s[3 * i + 2]);
+  x[42] = fmaxf(s[126], s[127]);
+  float y[15];
+#pragma unroll
+  for (int i = 0; i < 14; ++i) y[i] = max3(x[3 * i], x[3 * i + 1], x[3 * i + 2]);
+  y[14] = x[42];
+  float z[5];
+#pragma unroll
+  for (int i = 0; i < 5; ++i) z[i] = max3(y[3 * i], y[3 * i + 1], y[3 * i + 2]);
+  return max3(max3(z[0], z[1], z[2]), z[3], z[4]);
 }
 
 // V staging for bf16 inputs: Vh = fp16(V), per (head, chunk) flag = 1 if a finite V value of the
@@ -110,22 +123,33 @@ stage_v_f16(const uint4* __restrict__ V, uint4* __restrict__ Vh, int* __restrict
 }
 
 // Softmax of one S row already in registers: P = exp2(s*scale - m_sub) packed as 16-bit pairs into
-// two 32-word halves; returns the fp32 row sum of the unrounded values.
+// two 32-word halves (columns 0-63 and 64-127); returns the fp32 row sum of the unrounded values.
+// Scale-and-subtract and the row sum use packed two-lane fp32 instructions. The MUFU ex2 unit
+// (16 results per clock per SM) would otherwise bound this loop, so 3 of every 8 column pairs take
+// the polynomial exp2 on the FMA pipe instead (exp2_fma2).
 template <bool P_BF16>
 __device__ __forceinline__ float softmax_pack(const float (&s)[128], float scale_log2, float m_sub,
                                               uint32_t (&p_lo)[32], uint32_t (&p_hi)[32]) {
-  float rowsum = 0.f;
+  const float2 sc = make_float2(scale_log2, scale_log2), nm = make_float2(-m_sub, -m_sub);
+  float2 acc[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll
-  for (int c = 0; c < 32; ++c) {
-    const float p0 = ex2(fmaf(s[2 * c], scale_log2, -m_sub));
-    const float p1 = ex2(fmaf(s[2 * c + 1], scale_log2, -m_sub));
-    const float p2 = ex2(fmaf(s[64 + 2 * c], scale_log2, -m_sub));
-    const float p3 = ex2(fmaf(s[64 + 2 * c + 1], scale_log2, -m_sub));
-    rowsum += (p0 + p1) + (p2 + p3);
-    p_lo[c] = pack2<P_BF16>(p0, p1);
-    p_hi[c] = pack2<P_BF16>(p2, p3);
+  for (int c = 0; c < 64; ++c) {
+    float2 x = fma2(make_float2(s[2 * c], s[2 * c + 1]), sc, nm);
+    if ((c & 7) < 3) {
+      x = exp2_fma2(x);
+    } else {
+      x.x = ex2(x.x);
+      x.y = ex2(x.y);
+    }
+    acc[c & 3] = add2(acc[c & 3], x);
+    const uint32_t w = pack2<P_BF16>(x.x, x.y);
+    if (c < 32)
+      p_lo[c] = w;
+    else
+      p_hi[c - 32] = w;
   }
-  return rowsum;
+  const float2 t = add2(add2(acc[0], acc[1]), add2(acc[2], acc[3]));
+  return t.x + t.y;
 }
 
 // BF16: input/output dtype. vflags (bf16 only): per-(head, chunk) fp16-overflow flags of V.
@@ -195,27 +219,36 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
 
   if (warp == TMA_WARP || warp >= MMA_WARP + 2) {
     setmaxnreg_dec<kRegsProducer>();
-    if (warp == TMA_WARP && lane == 0) {
-      tma_prefetch_desc(&tmQ);
-      tma_prefetch_desc(&tmK);
-      tma_prefetch_desc(&tmV);
+    if (warp == TMA_WARP) {
+      // Producer: warp-uniform loop, one elected lane issues the copies.
       const CUtensorMap* tm_v = (BF16 && !pv_bf16) ? &tmVh : &tmV;
-      tma_prefetch_desc(tm_v);
       const int nq = has_b ? 2 : 1;
-      mbar_arrive_expect_tx(q_full(), nq * C::TILE_BYTES);
-      for (int g = 0; g < nq; ++g)
-        for (int c = 0; c < C::KBLK; ++c)
-          tma_load_3d(sbase + C::OFF_Q + g * C::TILE_BYTES + c * C::SUB_BYTES, &tmQ, q_full(), c * 64,
-                      row0 + g * BM, bh);
+      if (elect_one()) {
+        tma_prefetch_desc(&tmQ);
+        tma_prefetch_desc(&tmK);
+        tma_prefetch_desc(tm_v);
+        mbar_arrive_expect_tx(q_full(), nq * C::TILE_BYTES);
+        for (int g = 0; g < nq; ++g)
+          for (int c = 0; c < C::KBLK; ++c)
+            tma_load_3d(sbase + C::OFF_Q + g * C::TILE_BYTES + c * C::SUB_BYTES, &tmQ, q_full(), c * 64,
+                        row0 + g * BM, bh);
+      }
+      __syncwarp();
       int issued = 0;
       for (int t = 0; t < 2 * n_kv; ++t) {
         const int s = t % C::STAGES, r = t / C::STAGES;
-        if (r > 0 && !mbar_wait(kv_empty(s), (r - 1) & 1, abort_flag, status, kErrTmaWait)) break;
-        mbar_arrive_expect_tx(kv_full(s), C::TILE_BYTES);
+        if (r > 0) {
+          const bool ok = __all_sync(0xffffffffu, mbar_wait(kv_empty(s), (r - 1) & 1, abort_flag, status, kErrTmaWait));
+          if (!ok) break;
+        }
         const CUtensorMap* m = (t & 1) ? tm_v : &tmK;
         const int j = t >> 1;
-        for (int c = 0; c < C::KBLK; ++c)
-          tma_load_3d(sbase + C::OFF_KV + s * C::TILE_BYTES + c * C::SUB_BYTES, m, kv_full(s), c * 64, j * BN, bh);
+        if (elect_one()) {
+          mbar_arrive_expect_tx(kv_full(s), C::TILE_BYTES);
+          for (int c = 0; c < C::KBLK; ++c)
+            tma_load_3d(sbase + C::OFF_KV + s * C::TILE_BYTES + c * C::SUB_BYTES, m, kv_full(s), c * 64, j * BN, bh);
+        }
+        __syncwarp();
         issued = t + 1;
       }
       // Drain: every issued copy must land before this CTA's shared memory can be released.
@@ -225,72 +258,110 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
     }
   } else if (warp == MMA_WARP) {
     setmaxnreg_dec<kRegsProducer>();
-    if (lane == 0) {
+    // MMA issuer: the whole warp runs this warp-uniform loop and waits on the barriers; one elected
+    // lane (the same one every time, as tcgen05.commit tracks the issuing thread's MMAs) issues the
+    // tcgen05.mma and tcgen05.commit instructions.
+    {
       constexpr uint32_t idesc_qk = idesc_f16(BF16, BM, BN, false);
       const uint32_t idesc_pv = idesc_f16(pv_bf16, BM, D, true);
+      // Descriptors are formed as (region base descriptor) + (byte offset >> 4): the start-address
+      // field is the low 14 bits and every operand lies below 256 KB of shared memory, so the addition
+      // never carries out of the field.
+      const uint64_t dq = smem_desc_sw128(sbase + C::OFF_Q, 16, 1024);
+      const uint64_t dk = smem_desc_sw128(sbase + C::OFF_KV, 16, 1024);
+      const uint64_t dv = smem_desc_sw128(sbase + C::OFF_KV, C::SUB_BYTES, 1024);
       auto issue_qk = [&](int g, int stage) {
-        const uint32_t a0 = sbase + C::OFF_Q + g * C::TILE_BYTES;
-        const uint32_t b0 = sbase + C::OFF_KV + stage * C::TILE_BYTES;
+        const uint32_t a_off = (uint32_t)(g * C::TILE_BYTES) >> 4, b_off = (uint32_t)(stage * C::TILE_BYTES) >> 4;
         const uint32_t d_t = tmem + (g ? C::T_S1 : C::T_S0);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * C::SUB_BYTES + (kk & 3) * 32;
-          mma_ss(d_t, smem_desc_sw128(a0 + off, 16, 1024), smem_desc_sw128(b0 + off, 16, 1024), idesc_qk,
-                 kk > 0 ? 1u : 0u);
+          const uint32_t off = ((kk >> 2) * C::SUB_BYTES + (kk & 3) * 32) >> 4;
+          mma_ss(d_t, dq + (a_off + off), dk + (b_off + off), idesc_qk, kk > 0 ? 1u : 0u);
         }
       };
       auto issue_pv = [&](int g, int stage, bool acc) {
-        const uint32_t v0 = sbase + C::OFF_KV + stage * C::TILE_BYTES;
+        const uint32_t b_off = (uint32_t)(stage * C::TILE_BYTES) >> 4;
         const uint32_t d_t = tmem + (g ? C::T_O1 : C::T_O0);
         const uint32_t p_t = tmem + (g ? C::T_S1 : C::T_S0);
 #pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk)
-          mma_ts(d_t, p_t + kk * 8, smem_desc_sw128(v0 + kk * 2048, C::SUB_BYTES, 1024), idesc_pv,
-                 (acc || kk > 0) ? 1u : 0u);
+          mma_ts(d_t, p_t + kk * 8, dv + (b_off + kk * (2048 >> 4)), idesc_pv, (acc || kk > 0) ? 1u : 0u);
       };
-      const int ng = has_b ? 2 : 1;
-      bool ok = mbar_wait(q_full(), 0, abort_flag, status, kErrMmaWait);
-      int t = 0;  // index into the K0, V0, K1, V1, ... load sequence
-      if (ok) ok = mbar_wait(kv_full(0), 0, abort_flag, status, kErrMmaWait);
+      auto wait = [&](uint32_t bar, int parity) {
+        return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag, status, kErrMmaWait));
+      };
+      auto kv_wait = [&](int t) { return wait(kv_full(t % C::STAGES), (t / C::STAGES) & 1); };
+      // Issue order (ping-pong): tile A's P.V and its next Q.K^T go out as soon as softmax A is done,
+      // independently of tile B, so each softmax warpgroup overlaps the other tile's MMAs. S_g must not
+      // be overwritten before the P.V product has read P_g (P aliases S), so the issuer waits for that
+      // product's commit before issuing the next S_g; the other tile's MMAs keep the pipe busy.
+      bool ok = wait(q_full(), 0) && kv_wait(0);
       if (ok) {
         tc_fence_after();
-        for (int g = 0; g < ng; ++g) {
-          issue_qk(g, 0);
-          mma_commit(s_full(g));
+        if (elect_one()) {
+          issue_qk(0, 0);
+          mma_commit(s_full(0));
+          if (has_b) {
+            issue_qk(1, 0);
+            mma_commit(s_full(1));
+          }
+          mma_commit(kv_empty(0));
         }
-        mma_commit(kv_empty(0));
-        t = 1;
+        __syncwarp();
       }
       for (int j = 0; ok && j < n_kv; ++j) {
-        // O_g += P_g V_j
-        const int sv = t % C::STAGES;
-        if (!(ok = mbar_wait(kv_full(sv), (t / C::STAGES) & 1, abort_flag, status, kErrMmaWait))) break;
-        for (int g = 0; g < ng && ok; ++g) {
-          if (!(ok = mbar_wait(p_ready(g), j & 1, abort_flag, status, kErrMmaWait))) break;
-          tc_fence_after();
-          issue_pv(g, sv, j > 0);
-          mma_commit(o_done(g));
+        const int tv = 2 * j + 1, tk = 2 * j + 2;  // positions of V_j and K_{j+1} in the load sequence
+        const int sv = tv % C::STAGES, sk = tk % C::STAGES;
+        const bool more = j + 1 < n_kv;
+        if (!(ok = kv_wait(tv))) break;
+        // ---- tile A: O_A += P_A V_j, then S_A = Q_A K_{j+1}^T
+        if (!(ok = wait(p_ready(0), j & 1))) break;
+        tc_fence_after();
+        if (elect_one()) {
+          issue_pv(0, sv, j > 0);
+          mma_commit(o_done(0));
         }
-        if (!ok) break;
-        mma_commit(kv_empty(sv));
-        ++t;
-        if (j + 1 < n_kv) {
-          // S_g = Q_g K_{j+1}^T, once P_g (aliasing S_g) has been consumed by the PV product.
-          const int sk = t % C::STAGES;
-          if (!(ok = mbar_wait(kv_full(sk), (t / C::STAGES) & 1, abort_flag, status, kErrMmaWait))) break;
-          for (int g = 0; g < ng && ok; ++g) {
-            if (!(ok = mbar_wait(o_done(g), j & 1, abort_flag, status, kErrMmaWait))) break;
-            tc_fence_after();
-            issue_qk(g, sk);
-            mma_commit(s_full(g));
+        __syncwarp();
+        if (more) {
+          if (!(ok = kv_wait(tk) && wait(o_done(0), j & 1))) break;
+          tc_fence_after();
+          if (elect_one()) {
+            issue_qk(0, sk);
+            mma_commit(s_full(0));
           }
-          if (!ok) break;
-          mma_commit(kv_empty(sk));
-          ++t;
+          __syncwarp();
+        }
+        // ---- tile B
+        if (has_b) {
+          if (!(ok = wait(p_ready(1), j & 1))) break;
+          tc_fence_after();
+          if (elect_one()) {
+            issue_pv(1, sv, j > 0);
+            mma_commit(o_done(1));
+            mma_commit(kv_empty(sv));
+          }
+          __syncwarp();
+          if (more) {
+            if (!(ok = wait(o_done(1), j & 1))) break;
+            tc_fence_after();
+            if (elect_one()) {
+              issue_qk(1, sk);
+              mma_commit(s_full(1));
+              mma_commit(kv_empty(sk));
+            }
+            __syncwarp();
+          }
+        } else {
+          if (elect_one()) {
+            mma_commit(kv_empty(sv));
+            if (more) mma_commit(kv_empty(sk));
+          }
+          __syncwarp();
         }
       }
-      // Drain: all MMAs issued by this thread complete before TMEM is released.
-      mma_commit(drain_bar);
+      // Drain: all MMAs issued by the elected lane complete before TMEM is released.
+      if (elect_one()) mma_commit(drain_bar);
+      __syncwarp();
       mbar_wait_drain(drain_bar, 0);
     }
   } else {
@@ -321,10 +392,7 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
             if (col >= N || (causal && col > row)) s[c] = -CUDART_INF_F;
           }
         }
-        float mx = s[0];
-#pragma unroll
-        for (int c = 1; c < BN; ++c) mx = fmaxf(mx, s[c]);
-        const float m_new = mx * scale_log2;
+        const float m_new = row_max128(s) * scale_log2;
         if (j == 0) {
           m_used = m_new;
         } else {

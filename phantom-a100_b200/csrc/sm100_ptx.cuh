@@ -165,6 +165,29 @@ __device__ __forceinline__ void tmem_ld64_wait(uint32_t taddr, uint32_t (&r)[64]
       : "r"(taddr), "r"(taddr + 32)
       : "memory");
 }
+// 128 consecutive 32-bit TMEM columns: four 32-column loads in flight, one wait.
+__device__ __forceinline__ void tmem_ld128_wait(uint32_t taddr, uint32_t (&r)[128]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%128];\n\t"
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,"
+      "%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63}, [%129];\n\t"
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%64,%65,%66,%67,%68,%69,%70,%71,%72,%73,%74,%75,%76,%77,%78,%79,"
+      "%80,%81,%82,%83,%84,%85,%86,%87,%88,%89,%90,%91,%92,%93,%94,%95}, [%130];\n\t"
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%96,%97,%98,%99,%100,%101,%102,%103,%104,%105,%106,%107,%108,%109,%110,%111,"
+      "%112,%113,%114,%115,%116,%117,%118,%119,%120,%121,%122,%123,%124,%125,%126,%127}, [%131];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : PHANTOM_R8(0), PHANTOM_R8(8), PHANTOM_R8(16), PHANTOM_R8(24),
+        PHANTOM_R8(32), PHANTOM_R8(40), PHANTOM_R8(48), PHANTOM_R8(56),
+        PHANTOM_R8(64), PHANTOM_R8(72), PHANTOM_R8(80), PHANTOM_R8(88),
+        PHANTOM_R8(96), PHANTOM_R8(104), PHANTOM_R8(112), PHANTOM_R8(120)
+      : "r"(taddr), "r"(taddr + 32), "r"(taddr + 64), "r"(taddr + 96)
+      : "memory");
+}
 #undef PHANTOM_R8
 
 #define PHANTOM_S8(i) "r"(r[i]), "r"(r[i + 1]), "r"(r[i + 2]), "r"(r[i + 3]), \
@@ -190,6 +213,19 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16
 
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
+// One leader lane of a fully active warp (the same lane on every call); the other lanes get false.
+// Issuing tcgen05.mma / TMA from an elected lane of warp-uniform code keeps their operands in
+// uniform registers.
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "elect.sync _|p, 0xffffffff;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(pred));
+  return pred != 0;
+}
+
 // Warpgroup-wide register re-allocation (all four warps of a warpgroup execute the same one).
 template <int R>
 __device__ __forceinline__ void setmaxnreg_inc() {
@@ -210,6 +246,56 @@ __device__ __forceinline__ float ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// Three-input maximum (sm_100).
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// Packed two-lane fp32 arithmetic (one instruction for two values, sm_100).
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;"
+      : "=l"(d)
+      : "l"(*reinterpret_cast<uint64_t*>(&a)), "l"(*reinterpret_cast<uint64_t*>(&b)),
+        "l"(*reinterpret_cast<uint64_t*>(&c)));
+  return *reinterpret_cast<float2*>(&d);
+}
+__device__ __forceinline__ float2 add2(float2 a, float2 b) {
+  uint64_t d;
+  asm("add.f32x2 %0, %1, %2;"
+      : "=l"(d)
+      : "l"(*reinterpret_cast<uint64_t*>(&a)), "l"(*reinterpret_cast<uint64_t*>(&b)));
+  return *reinterpret_cast<float2*>(&d);
+}
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) {
+  uint64_t d;
+  asm("mul.f32x2 %0, %1, %2;"
+      : "=l"(d)
+      : "l"(*reinterpret_cast<uint64_t*>(&a)), "l"(*reinterpret_cast<uint64_t*>(&b)));
+  return *reinterpret_cast<float2*>(&d);
+}
+
+// 2^x for two values at once on the FMA pipe (x in [-125, 120]). Cody-Waite split x = j + f with
+// j = round(x) from the magic-number addition x + 1.5*2^23 (whose low mantissa bits then hold j) and
+// |f| <= 1/2; 2^f from a cubic fitted here by iteratively reweighted least squares to minimise the
+// maximum relative error on [-1/2, 1/2] (7.5e-5, a third of an fp16 half-ulp); j is added to the
+// exponent field of the result: bits(2^x) = bits(2^f) + (bits(x + 1.5*2^23) << 23) mod 2^32.
+__device__ __forceinline__ float2 exp2_fma2(float2 x) {
+  constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
+  x.x = fmaxf(x.x, -125.f);
+  x.y = fmaxf(x.y, -125.f);
+  const float2 t = add2(x, make_float2(kMagic, kMagic));
+  const float2 r = add2(t, make_float2(-kMagic, -kMagic));
+  const float2 f = fma2(r, make_float2(-1.f, -1.f), x);
+  float2 p = fma2(make_float2(0.0551716685f, 0.0551716685f), f, make_float2(0.2426111251f, 0.2426111251f));
+  p = fma2(p, f, make_float2(0.6932609677f, 0.6932609677f));
+  p = fma2(p, f, make_float2(0.9999280572f, 0.9999280572f));
+  return make_float2(__uint_as_float(__float_as_uint(p.x) + (__float_as_uint(t.x) << 23)),
+                     __uint_as_float(__float_as_uint(p.y) + (__float_as_uint(t.y) << 23)));
 }
 
 // Pack two fp32 values into one 32-bit word of two 16-bit values (lo in bits 0-15), round to nearest.
