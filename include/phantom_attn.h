@@ -59,6 +59,27 @@ int phantom_attn_fused_tc(const void* q, const void* k, const void* v, void* o, 
                           int head_dim, int dtype, int causal, void* stream);
 
 /*
+ * phantom_attn_fused_tc without any device-memory allocation, for callers that cannot allocate while
+ * they run: plugin hosts that own every byte of device memory and hand a plugin only its inputs and
+ * outputs, real-time loops that forbid allocator calls after start-up, and budgets where a hidden
+ * allocation could fail at the worst moment. No counterpart in the reference (its fused_tc needed no
+ * scratch; this library's bf16 path stages V as fp16 in scratch).
+ *
+ * Same arguments, checks, kernel and results as phantom_attn_fused_tc. Instead of allocating, it uses
+ * a file-scope 64 MiB device array that every GPU loading the library holds until the process exits:
+ * a 256-byte status word, then, for bf16 inputs, the fp16 copy of V (2 * BH * N * head_dim bytes) and
+ * 128 * BH bytes of overflow flags. bf16 inputs needing more than 64 MiB in all (BH * N * head_dim
+ * above about 33.5 million) are rejected with PHANTOM_ATTN_ERR_UNSUPPORTED; fp16 inputs need no
+ * scratch and have no such limit. The first call on a device sets that device up (it resolves the
+ * array's device address and zeroes the status word, synchronously), so make it before any stream
+ * capture. Every call on a device shares the array: calls that overlap on the GPU (different streams,
+ * or another thread) race on it and must be serialised by the caller. Bounded-wait expiries of this
+ * path are recorded in its own status word, which phantom_attn_device_status() does not read.
+ */
+int phantom_attn_fused_tc_noalloc(const void* q, const void* k, const void* v, void* o, int BH, int N,
+                                  int head_dim, int dtype, int causal, void* stream);
+
+/*
  * v3.1/v3.2 replacement. (br, bc) must be one of the reference's compiled tiles (64,32) (64,64)
  * (128,32) (128,64), else PHANTOM_ATTN_ERR_UNSUPPORTED with "not compiled". On sm_100a the work
  * runs on the tensor-core kernel above (its tile is fixed by the tcgen05 instruction shape); the

@@ -576,9 +576,42 @@ cudaError_t launch_d(const LaunchArgs& a, const CUtensorMap& mq, const CUtensorM
   return e != cudaSuccess ? e : ef;
 }
 
+// Same as launch_d, with the bf16 staging buffer [Vh | flags] supplied by the caller (no allocation).
+template <int D>
+cudaError_t launch_d_scratch(const LaunchArgs& a, const CUtensorMap& mq, const CUtensorMap& mk,
+                             const CUtensorMap& mv, void* scratch) {
+  if (a.dtype != PHANTOM_ATTN_BF16) return launch_t<D, false>(a, mq, mk, mv, mv, nullptr);
+  const size_t vh_bytes = (size_t)a.BH * a.N * D * 2;
+  void* vh = scratch;
+  int* flags = reinterpret_cast<int*>(static_cast<char*>(scratch) + vh_bytes);
+  const long long vec_per_head = (long long)a.N * D / 8;
+  tc::stage_v_f16<<<dim3(tc::kVChunks, a.BH), 256, 0, a.stream>>>(
+      static_cast<const uint4*>(a.v), static_cast<uint4*>(vh), flags, vec_per_head);
+  note_launch();
+  cudaError_t e = cudaGetLastError();
+  CUtensorMap mvh;
+  if (e == cudaSuccess && !make_map(&mvh, vh, a.BH, a.N, D, false)) e = cudaErrorInvalidValue;
+  if (e == cudaSuccess) e = launch_t<D, true>(a, mq, mk, mv, mvh, flags);
+  return e;
+}
+
 }  // namespace
 
 size_t fused_tc_smem_bytes(int d) { return d == 64 ? tc::Cfg<64>::SMEM_BYTES : tc::Cfg<128>::SMEM_BYTES; }
+
+size_t fused_tc_scratch_bytes(int BH, int N, int d, int dtype) {
+  if (dtype != PHANTOM_ATTN_BF16) return 0;
+  return (size_t)BH * N * d * 2 + (size_t)BH * tc::kVChunks * sizeof(int);
+}
+
+cudaError_t launch_fused_tc_sm100_scratch(const LaunchArgs& a, void* scratch) {
+  const bool bf16 = a.dtype == PHANTOM_ATTN_BF16;
+  CUtensorMap mq, mk, mv;
+  if (!make_map(&mq, a.q, a.BH, a.N, a.d, bf16) || !make_map(&mk, a.k, a.BH, a.N, a.d, bf16) ||
+      !make_map(&mv, a.v, a.BH, a.N, a.d, bf16))
+    return cudaErrorInvalidValue;
+  return a.d == 64 ? launch_d_scratch<64>(a, mq, mk, mv, scratch) : launch_d_scratch<128>(a, mq, mk, mv, scratch);
+}
 
 cudaError_t launch_fused_tc_sm100(const LaunchArgs& a) {
   const bool bf16 = a.dtype == PHANTOM_ATTN_BF16;

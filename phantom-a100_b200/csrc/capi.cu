@@ -159,6 +159,44 @@ int simt_entry(const char* name, const void* q, const void* k, const void* v, vo
   return run(name, launch_fused_simt, q, k, v, o, BH, N, d, dtype, causal, stream, dev);
 }
 
+// ------------------------------------------------------------------ entry point without allocation
+// Scratch of phantom_attn_fused_tc_noalloc, laid out as [status word (256 B) | fp16 copy of V |
+// V overflow flags]. A file-scope device array: every GPU that loads this library holds these 64 MiB
+// until the process exits. All calls on a device share it.
+constexpr size_t kNoAllocScratchBytes = size_t(64) << 20;
+constexpr size_t kNoAllocStatusBytes = 256;
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+std::mutex g_noalloc_mu;
+unsigned char* g_noalloc_ptr[kMaxDevices] = {};  // device address of g_noalloc_scratch, per device
+int g_noalloc_cc[kMaxDevices] = {};
+int g_noalloc_optin[kMaxDevices] = {};
+
+// Per-device set-up, once, with `dev` current: the device address of the static scratch (host code
+// only sees a stand-in for the array's name), the compute capability and the shared-memory limit,
+// and a zeroed status word. Nothing here allocates.
+int noalloc_setup(const char* name, int dev, unsigned char** scratch, int* cc, int* optin) {
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    int major = 0, minor = 0, opt = 0;
+    cudaError_t e;
+    if ((e = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev)) != cudaSuccess ||
+        (e = cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev)) != cudaSuccess ||
+        (e = cudaDeviceGetAttribute(&opt, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev)) != cudaSuccess)
+      return cuda_fail(name, e);
+    void* p = nullptr;
+    if ((e = cudaGetSymbolAddress(&p, g_noalloc_scratch)) != cudaSuccess) return cuda_fail(name, e);
+    if ((e = cudaMemset(p, 0, kNoAllocStatusBytes)) != cudaSuccess) return cuda_fail(name, e);
+    g_noalloc_cc[dev] = major * 10 + minor;
+    g_noalloc_optin[dev] = opt;
+    g_noalloc_ptr[dev] = static_cast<unsigned char*>(p);
+  }
+  *scratch = g_noalloc_ptr[dev];
+  *cc = g_noalloc_cc[dev];
+  *optin = g_noalloc_optin[dev];
+  return PHANTOM_ATTN_OK;
+}
+
 }  // namespace
 
 void note_launch() { ++g_launches; }
@@ -223,6 +261,50 @@ int phantom_attn_naive(const void* q, const void* k, const void* v, void* o, int
 int phantom_attn_tiled(const void* q, const void* k, const void* v, void* o, int BH, int N, int head_dim, int dtype,
                        int causal, void* stream) {
   return simt_entry("tiled", q, k, v, o, BH, N, head_dim, dtype, causal, stream);
+}
+
+int phantom_attn_fused_tc_noalloc(const void* q, const void* k, const void* v, void* o, int BH, int N,
+                                  int head_dim, int dtype, int causal, void* stream) {
+  const char* name = "fused_tc_noalloc";
+  if (BH <= 0 || N <= 0 || head_dim <= 0) return fail(PHANTOM_ATTN_ERR_INVALID, "%s: inputs must be non-empty", name);
+  if (dtype != PHANTOM_ATTN_F32 && dtype != PHANTOM_ATTN_F16 && dtype != PHANTOM_ATTN_BF16)
+    return fail(PHANTOM_ATTN_ERR_INVALID, "%s: unknown dtype code %d", name, dtype);
+  if (BH > 65535) return fail(PHANTOM_ATTN_ERR_UNSUPPORTED, "%s: batch*heads = %d exceeds 65535", name, BH);
+  if (dtype == PHANTOM_ATTN_F32)
+    return fail(PHANTOM_ATTN_ERR_UNSUPPORTED, "%s: float16 or bfloat16 only (tensor cores)", name);
+  if (head_dim != 64 && head_dim != 128)
+    return fail(PHANTOM_ATTN_ERR_UNSUPPORTED, "%s: only head dimension 64 and 128 are compiled (got %d)", name,
+                head_dim);
+  for (const void* p : {q, k, v, static_cast<const void*>(o)})
+    if (reinterpret_cast<uintptr_t>(p) % 16 != 0)
+      return fail(PHANTOM_ATTN_ERR_INVALID, "%s: inputs must be 16-byte aligned", name);
+  const size_t need = kNoAllocStatusBytes + fused_tc_scratch_bytes(BH, N, head_dim, dtype);
+  if (need > kNoAllocScratchBytes)
+    return fail(PHANTOM_ATTN_ERR_UNSUPPORTED,
+                "%s: bf16 inputs of B*H*N*d = %lld elements need %zu bytes of scratch; the static scratch holds "
+                "%zu bytes (use phantom_attn_fused_tc, which allocates, for larger bf16 inputs)",
+                name, (long long)BH * N * head_dim, need, kNoAllocScratchBytes);
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(name, e);
+  if (dev < 0 || dev >= kMaxDevices) return fail(PHANTOM_ATTN_ERR_INVALID, "%s: device %d out of range", name, dev);
+  unsigned char* scratch = nullptr;
+  int cc = 0, optin = 0;
+  int rc = noalloc_setup(name, dev, &scratch, &cc, &optin);
+  if (rc != PHANTOM_ATTN_OK) return rc;
+  const void* ptrs[4] = {q, k, v, o};
+  if ((rc = check_pointers(name, ptrs, dev)) != PHANTOM_ATTN_OK) return rc;
+  if (cc != 100)
+    return fail(PHANTOM_ATTN_ERR_UNSUPPORTED,
+                "%s: the tcgen05 kernel is compiled for sm_100a (B200); this GPU is sm_%d", name, cc);
+  if (fused_tc_smem_bytes(head_dim) > (size_t)optin)
+    return fail(PHANTOM_ATTN_ERR_UNSUPPORTED, "%s: needs %zu bytes of shared memory, GPU allows %d", name,
+                fused_tc_smem_bytes(head_dim), optin);
+  LaunchArgs a{q, k, v, o, BH, N, head_dim, dtype, causal != 0, static_cast<cudaStream_t>(stream),
+               reinterpret_cast<int*>(scratch)};
+  if ((e = launch_fused_tc_sm100_scratch(a, scratch + kNoAllocStatusBytes)) != cudaSuccess) return cuda_fail(name, e);
+  g_last_error.clear();
+  return PHANTOM_ATTN_OK;
 }
 
 int phantom_attn_device_status(int* status) {

@@ -22,6 +22,10 @@ struct LaunchArgs {
 cudaError_t launch_fused_tc_sm100(const LaunchArgs& a);
 // Dynamic shared memory the tensor-core kernel needs for head dim d.
 size_t fused_tc_smem_bytes(int d);
+// Tensor-core kernel with caller-supplied scratch for the bf16 V staging (no allocation inside);
+// fused_tc_scratch_bytes() is the size it needs (0 for fp16 inputs).
+cudaError_t launch_fused_tc_sm100_scratch(const LaunchArgs& a, void* scratch);
+size_t fused_tc_scratch_bytes(int BH, int N, int d, int dtype);
 
 // CUDA-core fp32-arithmetic kernel. Any d in [1, 256], dtype F32/F16/BF16.
 cudaError_t launch_fused_simt(const LaunchArgs& a);

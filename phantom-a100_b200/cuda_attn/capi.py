@@ -24,6 +24,7 @@ SIGNATURES = {
     "phantom_attn_version": (_I, []),
     "phantom_attn_last_error": (ctypes.c_char_p, []),
     "phantom_attn_fused_tc": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _I, _P]),
+    "phantom_attn_fused_tc_noalloc": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _I, _P]),
     "phantom_attn_fused_tuned": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _P]),
     "phantom_attn_fused": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _I, _P]),
     "phantom_attn_naive": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _I, _P]),
@@ -89,6 +90,10 @@ class CAPI:
 
     def fused_tc(self, q, k, v, o, causal=False, stream=None):
         return self._run(self.lib.phantom_attn_fused_tc, q, k, v, o, causal, stream)
+
+    def fused_tc_noalloc(self, q, k, v, o, causal=False, stream=None):
+        """fused_tc without device allocation (static scratch; bf16 limited to B*H*N*d <~ 33.5M)."""
+        return self._run(self.lib.phantom_attn_fused_tc_noalloc, q, k, v, o, causal, stream)
 
     def fused_tuned(self, q, k, v, o, causal=False, double_buffer=True, br=64, bc=32, stream=None):
         B, H, N, d = q.shape
