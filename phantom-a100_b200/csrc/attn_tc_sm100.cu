@@ -63,8 +63,9 @@ struct Cfg {
   static constexpr int OFF_Q = 0;
   static constexpr int OFF_KV = 2 * TILE_BYTES;
   static constexpr int OFF_BAR = OFF_KV + STAGES * TILE_BYTES;
-  // barriers: q_full, kv_full[STAGES], kv_empty[STAGES], s_full[2], p_ready[2], o_done[2], drain
-  static constexpr int NUM_BARS = 1 + 2 * STAGES + 7;
+  // barriers: q_full, kv_full[STAGES], kv_empty[STAGES], s_full[2], p_ready[2], o_done[2], drain,
+  // p_half[2]
+  static constexpr int NUM_BARS = 1 + 2 * STAGES + 9;
   static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;  // TMEM base address, abort flag
   static constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;  // + slack to align the base to 1024
   static constexpr uint32_t TMEM_COLS = 512;
@@ -122,32 +123,35 @@ stage_v_f16(const uint4* __restrict__ V, uint4* __restrict__ Vh, int* __restrict
   if (threadIdx.x == 0) flags[bh * kVChunks + blockIdx.x] = ovf;
 }
 
-// Softmax of one S row already in registers: P = exp2(s*scale - m_sub) packed as 16-bit pairs into
-// two 32-word halves (columns 0-63 and 64-127); returns the fp32 row sum of the unrounded values.
-// Scale-and-subtract and the row sum use packed two-lane fp32 instructions. The MUFU ex2 unit
-// (16 results per clock per SM) would otherwise bound this loop, so 3 of every 8 column pairs take
-// the polynomial exp2 on the FMA pipe instead (exp2_fma2).
-template <bool P_BF16>
-__device__ __forceinline__ float softmax_pack(const float (&s)[128], float scale_log2, float m_sub,
-                                              uint32_t (&p_lo)[32], uint32_t (&p_hi)[32]) {
+// Half a row of the softmax (columns H*64 .. H*64+63 of an S row held in registers): replaces each
+// score by p = exp2(s*scale - m_sub) in place (fp32, unrounded, kept for the row sum) and packs the
+// 64 values as 16-bit pairs into p[32]. Scale-and-subtract uses packed two-lane fp32 instructions; the
+// MUFU ex2 unit (16 results per clock per SM) would otherwise bound this loop, so 3 of every 8 column
+// pairs take the polynomial exp2 on the FMA pipe instead (exp2_fma2).
+template <bool P_BF16, int H>
+__device__ __forceinline__ void softmax_half(float (&s)[128], float scale_log2, float m_sub, uint32_t (&p)[32]) {
   const float2 sc = make_float2(scale_log2, scale_log2), nm = make_float2(-m_sub, -m_sub);
-  float2 acc[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll
-  for (int c = 0; c < 64; ++c) {
-    float2 x = fma2(make_float2(s[2 * c], s[2 * c + 1]), sc, nm);
+  for (int c = 0; c < 32; ++c) {
+    const int i = H * 64 + 2 * c;
+    float2 x = fma2(make_float2(s[i], s[i + 1]), sc, nm);
     if ((c & 7) < 3) {
       x = exp2_fma2(x);
     } else {
       x.x = ex2(x.x);
       x.y = ex2(x.y);
     }
-    acc[c & 3] = add2(acc[c & 3], x);
-    const uint32_t w = pack2<P_BF16>(x.x, x.y);
-    if (c < 32)
-      p_lo[c] = w;
-    else
-      p_hi[c - 32] = w;
+    s[i] = x.x;
+    s[i + 1] = x.y;
+    p[c] = pack2<P_BF16>(x.x, x.y);
   }
+}
+
+// Sum of the 128 unrounded p values of a row (packed two-lane adds, four independent chains).
+__device__ __forceinline__ float row_sum128(const float (&s)[128]) {
+  float2 acc[4] = {make_float2(s[0], s[1]), make_float2(s[2], s[3]), make_float2(s[4], s[5]), make_float2(s[6], s[7])};
+#pragma unroll
+  for (int c = 4; c < 64; ++c) acc[c & 3] = add2(acc[c & 3], make_float2(s[2 * c], s[2 * c + 1]));
   const float2 t = add2(add2(acc[0], acc[1]), add2(acc[2], acc[3]));
   return t.x + t.y;
 }
@@ -171,6 +175,7 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
   auto p_ready = [&](int g) { return bar0 + 8u * (3 + 2 * C::STAGES + g); };
   auto o_done = [&](int g) { return bar0 + 8u * (5 + 2 * C::STAGES + g); };
   const uint32_t drain_bar = bar0 + 8u * (7 + 2 * C::STAGES);
+  auto p_half = [&](int g) { return bar0 + 8u * (8 + 2 * C::STAGES + g); };
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 4);
   int* pv_bf16_flag = reinterpret_cast<int*>(smem + C::OFF_MISC + 8);
@@ -194,6 +199,7 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
     for (int g = 0; g < 2; ++g) {
       mbar_init(s_full(g), 1);
       mbar_init(p_ready(g), 128);
+      mbar_init(p_half(g), 128);
       mbar_init(o_done(g), 1);
     }
     mbar_init(drain_bar, 1);
@@ -279,22 +285,27 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
           mma_ss(d_t, dq + (a_off + off), dk + (b_off + off), idesc_qk, kk > 0 ? 1u : 0u);
         }
       };
-      auto issue_pv = [&](int g, int stage, bool acc) {
+      // P.V in two halves of 64 keys each (k steps 0-3 and 4-7), issued as each half of P lands.
+      auto issue_pv = [&](int g, int stage, bool acc, int half) {
         const uint32_t b_off = (uint32_t)(stage * C::TILE_BYTES) >> 4;
         const uint32_t d_t = tmem + (g ? C::T_O1 : C::T_O0);
         const uint32_t p_t = tmem + (g ? C::T_S1 : C::T_S0);
 #pragma unroll
-        for (int kk = 0; kk < BN / 16; ++kk)
+        for (int k = 0; k < BN / 32; ++k) {
+          const int kk = half * (BN / 32) + k;
           mma_ts(d_t, p_t + kk * 8, dv + (b_off + kk * (2048 >> 4)), idesc_pv, (acc || kk > 0) ? 1u : 0u);
+        }
       };
       auto wait = [&](uint32_t bar, int parity) {
         return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag, status, kErrMmaWait));
       };
       auto kv_wait = [&](int t) { return wait(kv_full(t % C::STAGES), (t / C::STAGES) & 1); };
-      // Issue order (ping-pong): tile A's P.V and its next Q.K^T go out as soon as softmax A is done,
-      // independently of tile B, so each softmax warpgroup overlaps the other tile's MMAs. S_g must not
-      // be overwritten before the P.V product has read P_g (P aliases S), so the issuer waits for that
-      // product's commit before issuing the next S_g; the other tile's MMAs keep the pipe busy.
+      // Issue order (ping-pong): tile A's P.V and its next Q.K^T go out as soon as softmax A hands P
+      // over, independently of tile B, so each softmax warpgroup overlaps the other tile's MMAs. The
+      // next S_g = Q_g K^T is issued right behind O_g += P_g V, although S_g's columns hold P_g: the
+      // tensor pipe executes one CTA's MMAs in issue order, so the P.V product has read P_g before the
+      // Q.K^T product writes there (the published FlashAttention-4 Blackwell kernel relies on the same
+      // ordering; the parity tests check the results bit for bit across reruns).
       bool ok = wait(q_full(), 0) && kv_wait(0);
       if (ok) {
         tc_fence_after();
@@ -315,15 +326,19 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
         const bool more = j + 1 < n_kv;
         if (!(ok = kv_wait(tv))) break;
         // ---- tile A: O_A += P_A V_j, then S_A = Q_A K_{j+1}^T
+        if (!(ok = wait(p_half(0), j & 1))) break;
+        tc_fence_after();
+        if (elect_one()) issue_pv(0, sv, j > 0, 0);
+        __syncwarp();
         if (!(ok = wait(p_ready(0), j & 1))) break;
         tc_fence_after();
         if (elect_one()) {
-          issue_pv(0, sv, j > 0);
+          issue_pv(0, sv, j > 0, 1);
           mma_commit(o_done(0));
         }
         __syncwarp();
         if (more) {
-          if (!(ok = kv_wait(tk) && wait(o_done(0), j & 1))) break;
+          if (!(ok = kv_wait(tk))) break;
           tc_fence_after();
           if (elect_one()) {
             issue_qk(0, sk);
@@ -333,17 +348,19 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
         }
         // ---- tile B
         if (has_b) {
+          if (!(ok = wait(p_half(1), j & 1))) break;
+          tc_fence_after();
+          if (elect_one()) issue_pv(1, sv, j > 0, 0);
+          __syncwarp();
           if (!(ok = wait(p_ready(1), j & 1))) break;
           tc_fence_after();
           if (elect_one()) {
-            issue_pv(1, sv, j > 0);
+            issue_pv(1, sv, j > 0, 1);
             mma_commit(o_done(1));
             mma_commit(kv_empty(sv));
           }
           __syncwarp();
           if (more) {
-            if (!(ok = wait(o_done(1), j & 1))) break;
-            tc_fence_after();
             if (elect_one()) {
               issue_qk(1, sk);
               mma_commit(s_full(1));
@@ -415,16 +432,26 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
           }
         }
         const float m_sub = m_used == -CUDART_INF_F ? 0.f : m_used;
-        uint32_t p_lo[32], p_hi[32];
+        // P for keys 0-63 goes out first: the MMA warp starts the P.V product on it while keys 64-127
+        // are still being exponentiated; the row sum comes after both halves are handed over.
+        uint32_t p[32];
         if (pv_bf16)
-          l += softmax_pack<true>(s, scale_log2, m_sub, p_lo, p_hi);
+          softmax_half<true, 0>(s, scale_log2, m_sub, p);
         else
-          l += softmax_pack<false>(s, scale_log2, m_sub, p_lo, p_hi);
-        tmem_st32(t_s, p_lo);
-        tmem_st32(t_s + 32, p_hi);
+          softmax_half<false, 0>(s, scale_log2, m_sub, p);
+        tmem_st32(t_s, p);
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(p_half(g));
+        if (pv_bf16)
+          softmax_half<true, 1>(s, scale_log2, m_sub, p);
+        else
+          softmax_half<false, 1>(s, scale_log2, m_sub, p);
+        tmem_st32(t_s + 32, p);
         tmem_wait_st();
         tc_fence_before();
         mbar_arrive(p_ready(g));
+        l += row_sum128(s);
       }
       if (ok) {
         ok = mbar_wait(o_done(g), (n_kv - 1) & 1, abort_flag, status, kErrEpilogueWait);
