@@ -9,6 +9,8 @@ Same names, signatures and error behaviour as the reference API (cuda_attn/__ini
                                                ring); fp16 or bf16, head dim 64 or 128.
   fused, naive, tiled                          fp32-arithmetic CUDA-core kernel; fp32/fp16/bf16, d <= 256.
   reference                                    fp32 math-backend SDPA, the ground truth of the tests.
+  fused_tc_host                                fused_tc for host (pinned) tensors: head chunks streamed
+                                               through the GPU with copies overlapping the kernel.
 
 The kernels live in libphantom_attn.so (C ABI: include/phantom_attn.h); `_C` is the PyTorch
 extension over it. There is no CPU fallback: if the extension is missing, every kernel call raises.
@@ -88,6 +90,8 @@ def device_status() -> int:
     return _ext().device_status()
 
 
+from .pipeline import fused_tc_host  # noqa: E402  (host-resident inputs, copies overlapped with compute)
+
 # Every version, in the order the reference builds them.
 KERNELS = {"naive": naive, "tiled": tiled, "fused": fused,
            "fused_vec": fused_vec, "fused_db": fused_db, "fused_tc": fused_tc}
@@ -95,4 +99,4 @@ KERNELS = {"naive": naive, "tiled": tiled, "fused": fused,
 FP16_ONLY = {"fused_vec", "fused_db", "fused_tc"}
 
 __all__ = ["naive", "tiled", "fused", "fused_tuned", "fused_vec", "fused_db", "fused_tc",
-           "reference", "KERNELS", "FP16_ONLY", "device_status"]
+           "reference", "KERNELS", "FP16_ONLY", "device_status", "fused_tc_host"]

@@ -1,0 +1,100 @@
+"""Attention over host-resident tensors: the GPU work is pipelined with the host link.
+
+    o = cuda_attn.fused_tc_host(q, k, v)      # q, k, v: (B, H, N, d) pinned CPU tensors -> O on the host
+
+Heads are independent, so the B*H heads are cut into chunks and streamed through two device slots on three
+CUDA streams: while chunk i is attended on the compute stream, chunk i+1 is copied host->device and chunk
+i-1 device->host. The host link (~50 GB/s per direction) rather than the kernel then bounds the call, and
+the two directions overlap each other. Each chunk runs the same C-ABI entry point as fused_tc.
+"""
+from __future__ import annotations
+
+import math
+import threading
+
+import torch
+
+from .capi import CAPI
+
+_LOCAL = threading.local()
+
+
+def _lib() -> CAPI:
+    lib = getattr(_LOCAL, "lib", None)
+    if lib is None:
+        lib = _LOCAL.lib = CAPI()
+    return lib
+
+
+def _streams(device: torch.device):
+    key = ("streams", device.index)
+    s = getattr(_LOCAL, "streams", {})
+    if key not in s:
+        s[key] = tuple(torch.cuda.Stream(device=device) for _ in range(3))
+        _LOCAL.streams = s
+    return s[key]
+
+
+def fused_tc_host(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool = False,
+                  out: torch.Tensor | None = None, chunks: int = 8, device: int | torch.device | None = None,
+                  synchronize: bool = True) -> torch.Tensor:
+    """fused_tc for (B, H, N, d) CPU tensors (pin them for overlap; pageable memory works but serialises
+    the copies). Returns O as a CPU tensor of the input dtype (`out` if given, pinned otherwise). With
+    synchronize=False the call returns once the work is queued; the current CUDA stream of `device` is
+    ordered after the last copy, so synchronising it (or an event recorded on it) makes O valid."""
+    for t in (q, k, v):
+        if t.is_cuda:
+            raise RuntimeError("fused_tc_host: inputs must be CPU tensors (use fused_tc for device tensors)")
+        if not t.is_contiguous():
+            raise RuntimeError("fused_tc_host: inputs must be contiguous")
+        if t.dim() != 4:
+            raise RuntimeError("fused_tc_host: inputs must be shaped (B, H, N, d)")
+        if t.dtype != q.dtype:
+            raise RuntimeError("fused_tc_host: q, k, v must share a dtype")
+    if q.shape != k.shape or q.shape != v.shape:
+        raise RuntimeError("fused_tc_host: q, k, v must have the same shape")
+    B, H, N, d = q.shape
+    BH = B * H
+    dev = torch.device("cuda", torch.cuda.current_device() if device is None else torch.device(device).index or 0)
+    if out is None:
+        out = torch.empty(q.shape, dtype=q.dtype, pin_memory=True)
+    hq, hk, hv, ho = (x.view(BH, N, d) for x in (q, k, v, out))
+    per = max(1, math.ceil(BH / max(1, chunks)))
+    n_chunks = math.ceil(BH / per)
+    lib = _lib()
+    with torch.cuda.device(dev):
+        h2d, comp, d2h = _streams(dev)
+        cur = torch.cuda.current_stream(dev)
+        slots = [[torch.empty((per, N, d), dtype=q.dtype, device=dev) for _ in range(4)] for _ in range(2)]
+        loaded = [torch.cuda.Event() for _ in range(2)]
+        computed = [torch.cuda.Event() for _ in range(2)]
+        freed = [torch.cuda.Event() for _ in range(2)]
+        h2d.wait_stream(cur)  # inputs written by earlier work on the caller's stream are visible
+        for i in range(n_chunks):
+            s = i % 2
+            a, b = i * per, min(BH, (i + 1) * per)
+            n = b - a
+            dq, dk, dv, do = (x[:n] for x in slots[s])
+            if i >= 2:
+                h2d.wait_event(freed[s])
+            with torch.cuda.stream(h2d):
+                dq.copy_(hq[a:b], non_blocking=True)
+                dk.copy_(hk[a:b], non_blocking=True)
+                dv.copy_(hv[a:b], non_blocking=True)
+                loaded[s].record(h2d)
+            comp.wait_event(loaded[s])
+            lib.fused_tc(dq.unsqueeze(0), dk.unsqueeze(0), dv.unsqueeze(0), do.unsqueeze(0), causal=causal,
+                         stream=comp)
+            computed[s].record(comp)
+            d2h.wait_event(computed[s])
+            with torch.cuda.stream(d2h):
+                ho[a:b].copy_(do, non_blocking=True)
+                freed[s].record(d2h)
+        cur.wait_stream(d2h)
+        for t in (slots[0] + slots[1]):
+            t.record_stream(h2d)
+            t.record_stream(comp)
+            t.record_stream(d2h)
+        if synchronize:
+            cur.synchronize()
+    return out

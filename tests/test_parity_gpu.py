@@ -163,3 +163,18 @@ def test_config5_sweep(capi, n, d):
 def test_causal_full_size(capi, dtype):
     q, k, v = make_qkv(1, 4, 4096, 128, dtype, seed=21)
     check_full_size(capi, q, k, v, True, torch_dtype_name(dtype), heads=[0, 3], n_rows=64)
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("chunks", [1, 3, 8])
+def test_host_pipeline_equals_device_call(capi, dtype, chunks):
+    """fused_tc_host streams head chunks through the GPU; heads are independent, so the result must equal
+    the device-resident call bit for bit, for any chunking (including a ragged last chunk)."""
+    import cuda_attn
+    q, k, v = make_qkv(2, 5, 700, 128, dtype, seed=31)
+    o_dev = torch.empty_like(q)
+    capi.fused_tc(q, k, v, o_dev, causal=True)
+    hq, hk, hv = (x.cpu().pin_memory() for x in (q, k, v))
+    o_host = cuda_attn.fused_tc_host(hq, hk, hv, causal=True, chunks=chunks)
+    assert not o_host.is_cuda and o_host.dtype == dtype
+    assert torch.equal(o_host, o_dev.cpu())
