@@ -130,3 +130,14 @@ def test_misaligned_pointer_rejected():
     q = base[4:].view(1, 1, 64, 64)  # 8-byte offset
     with pytest.raises(RuntimeError, match="16-byte aligned"):
         cuda_attn.fused_tc(q, q, q)
+
+
+def test_sweep_tool_writes_gated_rows(tmp_path):
+    """cuda_attn.sweep (the reference's bench/benchmark.py on B200): every row passes the correctness gate."""
+    import csv
+    from cuda_attn import sweep
+    out = tmp_path / "s.csv"
+    assert sweep.main(["--ns", "128", "640", "--dims", "64", "128", "--heads", "4", "--iters", "3", "--warmup", "1",
+                       "--impls", "fused_tc", "fused", "--out", str(out)]) == 0
+    rows = list(csv.DictReader(open(out)))
+    assert len(rows) == 8 and all(r["status"] == "ok" for r in rows), rows
