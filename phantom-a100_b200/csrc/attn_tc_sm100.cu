@@ -15,16 +15,23 @@
 //   * One CTA owns two 128-row Q tiles (A, B) of one (batch, head) and streams K/V tiles of 128 keys.
 //   * Warp 9 (one thread) is the TMA producer: Q tiles once, then K_0, V_0, K_1, V_1, ... into a ring
 //     of STAGES shared-memory slots (128-byte swizzle), completion tracked by mbarrier tx bytes.
-//   * Warp 8 (one thread) issues every tcgen05.mma: S_g = Q_g K_j^T (both operands in shared memory,
-//     fp32 accumulator in TMEM, 128 lanes x 128 columns) and O_g += P_g V_j (P read from TMEM,
-//     V from shared memory as an MN-major operand, accumulator in TMEM). Commits go to mbarriers.
+//   * Warp 8 (one thread) issues the S_g = Q_g K_j^T products (both operands in shared memory, fp32
+//     accumulator in TMEM, 128 lanes x 128 columns); warp 10 (one thread) issues O_g += P_g V_j
+//     (P read from TMEM, V from shared memory as an MN-major operand, accumulator in TMEM). Commits
+//     go to mbarriers. Two issuers because an issuing thread blocks while the tensor core's
+//     instruction queue is full: with one, an S product waiting behind a P.V product (or the
+//     reverse) stalled the other chain.
 //   * Warps 0-3 / 4-7 are the softmax warpgroups of tiles A / B: thread t owns query row t = TMEM
-//     lane t, so the row max and row sum need no shuffles. Each thread loads its S row from TMEM,
-//     masks, takes the max, rescales its O row in TMEM only when the max grew by more than 2^8
-//     (exact: every P and l of a row use the same reference max), computes P with ex2, writes it
-//     back into the S columns as packed 16-bit pairs (the A operand of the next MMA), then arrives.
-//   * While one warpgroup runs its softmax the tensor core works on the other tile's MMAs.
-//   * TMEM: S_A [0,128), S_B [128,256), O_A [256,256+d), O_B [256+d,256+2d); P_g aliases S_g.
+//     lane t, so the row max and row sum need no shuffles. Each thread loads its S row from TMEM and
+//     releases the S columns at once, masks, takes the max, rescales its O row in TMEM only when the
+//     max grew by more than 2^8 (exact: every P and l of a row use the same reference max), computes
+//     P with ex2 and writes it into its tile's P columns as packed 16-bit pairs (the A operand of
+//     the P.V product), then arrives.
+//   * P never shares columns with S, so the next S product runs while the softmax of the current K/V
+//     tile still computes; each softmax warpgroup then goes from tile to tile without waiting for
+//     its own P.V product (only for the previous one, before it overwrites P and rescales O).
+//   * TMEM (512 columns): d = 128: S [0,128) used by tiles A and B in turn, P_A [128,192),
+//     P_B [192,256), O_A [256,384), O_B [384,512); d = 64: O_A, O_B, then S_A, S_B, P_A, P_B.
 //   * Every mbarrier wait is bounded; on expiry the CTA drains its in-flight copies and MMAs,
 //     frees TMEM, records the failure in the device status word and exits.
 #include <cuda.h>
@@ -40,9 +47,9 @@ namespace phantom {
 namespace tc {
 
 constexpr int BM = 128;  // query rows per Q tile = TMEM lanes
-constexpr int BN = 128;  // keys per K/V tile
-constexpr int MMA_WARP = 8;
-constexpr int TMA_WARP = 9;          // warps 10-11 complete the producer warpgroup and idle
+constexpr int MMA_WARP = 8;          // issues the Q.K^T products
+constexpr int TMA_WARP = 9;
+constexpr int PV_WARP = 10;          // issues the P.V products; warp 11 completes the producer warpgroup
 constexpr int NUM_THREADS = 384;
 // Register split (setmaxnreg): the kernel launches at 168 registers/thread (384 threads, 1 CTA/SM).
 // The producer warpgroup drops to 72 and the two softmax warpgroups rise to 216:
@@ -54,45 +61,65 @@ constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale O only when th
 // Status-word bits (which wait expired).
 constexpr int kErrTmaWait = 1, kErrMmaWait = 2, kErrSoftmaxWait = 4, kErrEpilogueWait = 8;
 
+// TMEM plan per head dimension (K/V tiles of BN = 128 keys). P (the probabilities as packed 16-bit
+// pairs, the A operand of O += P V) never shares columns with S (fp32 scores), so a Q.K^T product is
+// issued as soon as the softmax has read the previous S into registers, while O += P V of the
+// previous tile still reads P:
+//   d = 128: one S region that Q tiles A and B use in turn (A, B, A, B, ...):
+//            S [0,128)  P_A [128,192)  P_B [192,256)  O_A [256,384)  O_B [384,512)
+//   d =  64: an S region per Q tile:
+//            O_A [0,64)  O_B [64,128)  S_A [128,256)  S_B [256,384)  P_A [384,448)  P_B [448,512)
 template <int D>
 struct Cfg {
+  static constexpr bool SHARED_S = D == 128;
+  static constexpr int BN = 128;                     // keys per K/V tile
   static constexpr int KBLK = D / 64;                // 64-element (128-byte) swizzle blocks across d
-  static constexpr int SUB_BYTES = BM * 128;         // one 64-column block of a 128-row tile
-  static constexpr int TILE_BYTES = BM * D * 2;      // one Q, K or V tile
+  static constexpr int Q_SUB = BM * 128;             // one 64-column block of a Q tile
+  static constexpr int KV_SUB = BN * 128;            // one 64-column block of a K or V tile
+  static constexpr int Q_TILE = BM * D * 2;
+  static constexpr int KV_TILE = BN * D * 2;
   static constexpr int STAGES = D == 128 ? 4 : 8;    // K/V ring slots
   static constexpr int OFF_Q = 0;
-  static constexpr int OFF_KV = 2 * TILE_BYTES;
-  static constexpr int OFF_BAR = OFF_KV + STAGES * TILE_BYTES;
-  // barriers: q_full, kv_full[STAGES], kv_empty[STAGES], s_full[2], p_ready[2], o_done[2], drain,
-  // p_half[2]
-  static constexpr int NUM_BARS = 1 + 2 * STAGES + 9;
-  static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;  // TMEM base address, abort flag
+  static constexpr int OFF_KV = 2 * Q_TILE;
+  static constexpr int OFF_BAR = OFF_KV + STAGES * KV_TILE;
+  // barriers: q_full, kv_full[STAGES], kv_empty[STAGES], s_full[2], s_free[2], p_ready[2], o_done[2],
+  // drain (S issuer), drain (P.V issuer)
+  static constexpr int NUM_BARS = 1 + 2 * STAGES + 10;
+  static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;  // TMEM base address, abort flag, P precision
   static constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;  // + slack to align the base to 1024
   static constexpr uint32_t TMEM_COLS = 512;
-  static constexpr uint32_t T_S0 = 0, T_S1 = 128, T_O0 = 256, T_O1 = 256 + D;
+  static constexpr uint32_t T_S0 = SHARED_S ? 0 : 2 * D, T_S1 = SHARED_S ? 0 : 2 * D + BN;
+  static constexpr uint32_t T_P0 = SHARED_S ? BN : 2 * D + 2 * BN, T_P1 = T_P0 + BN / 2;
+  static constexpr uint32_t T_O0 = SHARED_S ? 2 * BN : 0, T_O1 = T_O0 + D;
+  static_assert(T_P1 + BN / 2 <= TMEM_COLS, "TMEM plan exceeds 512 columns");
 };
 
-__device__ __forceinline__ void ld128(uint32_t taddr, float (&s)[128]) {
-  uint32_t r[128];
-  tmem_ld128_wait(taddr, r);
+template <int N>
+__device__ __forceinline__ void ld_row(uint32_t taddr, float (&s)[N]) {
+  if constexpr (N == 64) {
+    uint32_t r[64];
+    tmem_ld64_wait(taddr, r);
 #pragma unroll
-  for (int i = 0; i < 128; ++i) s[i] = __uint_as_float(r[i]);
+    for (int i = 0; i < 64; ++i) s[i] = __uint_as_float(r[i]);
+  } else {
+    uint32_t r[128];
+    tmem_ld128_wait(taddr, r);
+#pragma unroll
+    for (int i = 0; i < 128; ++i) s[i] = __uint_as_float(r[i]);
+  }
 }
 
-// Maximum of 128 values: a 5-level tree of 3-input maxima (64 instructions, short dependency chain).
-__device__ __forceinline__ float row_max128(const float (&s)[128]) {
-  float x[43];
+// Maximum of N values: eight running 3-input maxima and a short final tree.
+template <int N>
+__device__ __forceinline__ float row_max(const float (&s)[N]) {
+  float a[8];
 #pragma unroll
-  for (int i = 0; i < 42; ++i) x[i] = max3(s[3 * i], s[3 * i + 1], s[3 * i + 2]);
-  x[42] = fmaxf(s[126], s[127]);
-  float y[15];
+  for (int k = 0; k < 8; ++k) a[k] = fmaxf(s[k], s[k + 8]);
 #pragma unroll
-  for (int i = 0; i < 14; ++i) y[i] = max3(x[3 * i], x[3 * i + 1], x[3 * i + 2]);
-  y[14] = x[42];
-  float z[5];
+  for (int i = 16; i < N; i += 16)
 #pragma unroll
-  for (int i = 0; i < 5; ++i) z[i] = max3(y[3 * i], y[3 * i + 1], y[3 * i + 2]);
-  return max3(max3(z[0], z[1], z[2]), z[3], z[4]);
+    for (int k = 0; k < 8; ++k) a[k] = max3(a[k], s[i + k], s[i + 8 + k]);
+  return fmaxf(max3(a[0], a[1], a[2]), max3(a[3], a[4], max3(a[5], a[6], a[7])));
 }
 
 // V staging for bf16 inputs: Vh = fp16(V), per (head, chunk) flag = 1 if a finite V value of the
@@ -123,36 +150,26 @@ stage_v_f16(const uint4* __restrict__ V, uint4* __restrict__ Vh, int* __restrict
   if (threadIdx.x == 0) flags[bh * kVChunks + blockIdx.x] = ovf;
 }
 
-// Half a row of the softmax (columns H*64 .. H*64+63 of an S row held in registers): replaces each
-// score by p = exp2(s*scale - m_sub) in place (fp32, unrounded, kept for the row sum) and packs the
-// 64 values as 16-bit pairs into p[32]. Scale-and-subtract uses packed two-lane fp32 instructions; the
-// MUFU ex2 unit (16 results per clock per SM) would otherwise bound this loop, so 3 of every 8 column
-// pairs take the polynomial exp2 on the FMA pipe instead (exp2_fma2).
-template <bool P_BF16, int H>
-__device__ __forceinline__ void softmax_half(float (&s)[128], float scale_log2, float m_sub, uint32_t (&p)[32]) {
+// p = exp2(s*scale - m_sub) for 64 scores of a row (s[OFF .. OFF+63]), packed as 16-bit pairs into p[32];
+// returns the sum of the unrounded fp32 values. Column pairs c with c % 8 in {0, 2, 5} take the
+// polynomial exp2 on the FMA pipe, the others the MUFU ex2 unit (16 results per clock per SM).
+template <bool P_BF16, int OFF, int N>
+__device__ __forceinline__ float softmax64(const float (&s)[N], float scale_log2, float m_sub, uint32_t (&p)[32]) {
   const float2 sc = make_float2(scale_log2, scale_log2), nm = make_float2(-m_sub, -m_sub);
+  float2 acc[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll
   for (int c = 0; c < 32; ++c) {
-    const int i = H * 64 + 2 * c;
-    float2 x = fma2(make_float2(s[i], s[i + 1]), sc, nm);
-    if ((c & 7) < 3) {
+    float2 x = fma2(make_float2(s[OFF + 2 * c], s[OFF + 2 * c + 1]), sc, nm);
+    if ((0x25 >> (c & 7)) & 1) {
       x = exp2_fma2(x);
     } else {
       x.x = ex2(x.x);
       x.y = ex2(x.y);
     }
-    s[i] = x.x;
-    s[i + 1] = x.y;
+    acc[c & 1] = add2(acc[c & 1], x);
     p[c] = pack2<P_BF16>(x.x, x.y);
   }
-}
-
-// Sum of the 128 unrounded p values of a row (packed two-lane adds, four independent chains).
-__device__ __forceinline__ float row_sum128(const float (&s)[128]) {
-  float2 acc[4] = {make_float2(s[0], s[1]), make_float2(s[2], s[3]), make_float2(s[4], s[5]), make_float2(s[6], s[7])};
-#pragma unroll
-  for (int c = 4; c < 64; ++c) acc[c & 3] = add2(acc[c & 3], make_float2(s[2 * c], s[2 * c + 1]));
-  const float2 t = add2(add2(acc[0], acc[1]), add2(acc[2], acc[3]));
+  const float2 t = add2(acc[0], acc[1]);
   return t.x + t.y;
 }
 
@@ -164,6 +181,7 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
             const int* __restrict__ vflags, uint16_t* __restrict__ O, int N, float scale_log2, int causal,
             int* __restrict__ status) {
   using C = Cfg<D>;
+  constexpr int BN = C::BN;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sbase = smem_u32(smem);
@@ -172,10 +190,11 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
   auto kv_full = [&](int s) { return bar0 + 8u * (1 + s); };
   auto kv_empty = [&](int s) { return bar0 + 8u * (1 + C::STAGES + s); };
   auto s_full = [&](int g) { return bar0 + 8u * (1 + 2 * C::STAGES + g); };
-  auto p_ready = [&](int g) { return bar0 + 8u * (3 + 2 * C::STAGES + g); };
-  auto o_done = [&](int g) { return bar0 + 8u * (5 + 2 * C::STAGES + g); };
-  const uint32_t drain_bar = bar0 + 8u * (7 + 2 * C::STAGES);
-  auto p_half = [&](int g) { return bar0 + 8u * (8 + 2 * C::STAGES + g); };
+  auto s_free = [&](int g) { return bar0 + 8u * (3 + 2 * C::STAGES + g); };
+  auto p_ready = [&](int g) { return bar0 + 8u * (5 + 2 * C::STAGES + g); };
+  auto o_done = [&](int g) { return bar0 + 8u * (7 + 2 * C::STAGES + g); };
+  const uint32_t drain_bar = bar0 + 8u * (9 + 2 * C::STAGES);
+  const uint32_t drain_pv_bar = bar0 + 8u * (10 + 2 * C::STAGES);
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 4);
   int* pv_bf16_flag = reinterpret_cast<int*>(smem + C::OFF_MISC + 8);
@@ -198,11 +217,12 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
     }
     for (int g = 0; g < 2; ++g) {
       mbar_init(s_full(g), 1);
+      mbar_init(s_free(g), 128);
       mbar_init(p_ready(g), 128);
-      mbar_init(p_half(g), 128);
       mbar_init(o_done(g), 1);
     }
     mbar_init(drain_bar, 1);
+    mbar_init(drain_pv_bar, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -223,21 +243,21 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
   const uint32_t tmem = *tmem_holder;
   const bool pv_bf16 = BF16 && *pv_bf16_flag != 0;  // CTA-uniform
 
-  if (warp == TMA_WARP || warp >= MMA_WARP + 2) {
+  if (warp == TMA_WARP || warp == PV_WARP + 1) {
     setmaxnreg_dec<kRegsProducer>();
     if (warp == TMA_WARP) {
-      // Producer: warp-uniform loop, one elected lane issues the copies.
+      // Producer: Q tiles once, then K_0, V_0, K_1, V_1, ... into the ring (warp-uniform loop, one
+      // elected lane issues the copies).
       const CUtensorMap* tm_v = (BF16 && !pv_bf16) ? &tmVh : &tmV;
       const int nq = has_b ? 2 : 1;
       if (elect_one()) {
         tma_prefetch_desc(&tmQ);
         tma_prefetch_desc(&tmK);
         tma_prefetch_desc(tm_v);
-        mbar_arrive_expect_tx(q_full(), nq * C::TILE_BYTES);
+        mbar_arrive_expect_tx(q_full(), nq * C::Q_TILE);
         for (int g = 0; g < nq; ++g)
           for (int c = 0; c < C::KBLK; ++c)
-            tma_load_3d(sbase + C::OFF_Q + g * C::TILE_BYTES + c * C::SUB_BYTES, &tmQ, q_full(), c * 64,
-                        row0 + g * BM, bh);
+            tma_load_3d(sbase + C::OFF_Q + g * C::Q_TILE + c * C::Q_SUB, &tmQ, q_full(), c * 64, row0 + g * BM, bh);
       }
       __syncwarp();
       int issued = 0;
@@ -250,9 +270,9 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
         const CUtensorMap* m = (t & 1) ? tm_v : &tmK;
         const int j = t >> 1;
         if (elect_one()) {
-          mbar_arrive_expect_tx(kv_full(s), C::TILE_BYTES);
+          mbar_arrive_expect_tx(kv_full(s), C::KV_TILE);
           for (int c = 0; c < C::KBLK; ++c)
-            tma_load_3d(sbase + C::OFF_KV + s * C::TILE_BYTES + c * C::SUB_BYTES, m, kv_full(s), c * 64, j * BN, bh);
+            tma_load_3d(sbase + C::OFF_KV + s * C::KV_TILE + c * C::KV_SUB, m, kv_full(s), c * 64, j * BN, bh);
         }
         __syncwarp();
         issued = t + 1;
@@ -262,11 +282,14 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
       for (int t = (issued > C::STAGES ? issued - C::STAGES : 0); t < issued; ++t)
         mbar_wait_drain(kv_full(t % C::STAGES), (t / C::STAGES) & 1);
     }
-  } else if (warp == MMA_WARP) {
+  } else if (warp == MMA_WARP || warp == PV_WARP) {
     setmaxnreg_dec<kRegsProducer>();
-    // MMA issuer: the whole warp runs this warp-uniform loop and waits on the barriers; one elected
-    // lane (the same one every time, as tcgen05.commit tracks the issuing thread's MMAs) issues the
-    // tcgen05.mma and tcgen05.commit instructions.
+    // Two MMA issuers, each a warp-uniform loop in which one elected lane (the same one every time, as
+    // tcgen05.commit tracks the issuing thread's MMAs) issues tcgen05.mma and tcgen05.commit: warp 8
+    // the S = Q K^T products, warp 10 the O += P V products. An issuer blocks while the tensor core's
+    // instruction queue is full, so separate issuers keep the two dependency chains from waiting on
+    // each other; they touch disjoint TMEM columns (S / P, O), and every cross dependency goes through
+    // the softmax warps and the barriers below.
     {
       constexpr uint32_t idesc_qk = idesc_f16(BF16, BM, BN, false);
       const uint32_t idesc_pv = idesc_f16(pv_bf16, BM, D, true);
@@ -275,114 +298,86 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
       // never carries out of the field.
       const uint64_t dq = smem_desc_sw128(sbase + C::OFF_Q, 16, 1024);
       const uint64_t dk = smem_desc_sw128(sbase + C::OFF_KV, 16, 1024);
-      const uint64_t dv = smem_desc_sw128(sbase + C::OFF_KV, C::SUB_BYTES, 1024);
-      auto issue_qk = [&](int g, int stage) {
-        const uint32_t a_off = (uint32_t)(g * C::TILE_BYTES) >> 4, b_off = (uint32_t)(stage * C::TILE_BYTES) >> 4;
-        const uint32_t d_t = tmem + (g ? C::T_S1 : C::T_S0);
-#pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = ((kk >> 2) * C::SUB_BYTES + (kk & 3) * 32) >> 4;
-          mma_ss(d_t, dq + (a_off + off), dk + (b_off + off), idesc_qk, kk > 0 ? 1u : 0u);
-        }
-      };
-      // P.V in two halves of 64 keys each (k steps 0-3 and 4-7), issued as each half of P lands.
-      auto issue_pv = [&](int g, int stage, bool acc, int half) {
-        const uint32_t b_off = (uint32_t)(stage * C::TILE_BYTES) >> 4;
-        const uint32_t d_t = tmem + (g ? C::T_O1 : C::T_O0);
-        const uint32_t p_t = tmem + (g ? C::T_S1 : C::T_S0);
-#pragma unroll
-        for (int k = 0; k < BN / 32; ++k) {
-          const int kk = half * (BN / 32) + k;
-          mma_ts(d_t, p_t + kk * 8, dv + (b_off + kk * (2048 >> 4)), idesc_pv, (acc || kk > 0) ? 1u : 0u);
-        }
-      };
+      const uint64_t dv = smem_desc_sw128(sbase + C::OFF_KV, C::KV_SUB, 1024);
       auto wait = [&](uint32_t bar, int parity) {
         return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag, status, kErrMmaWait));
       };
       auto kv_wait = [&](int t) { return wait(kv_full(t % C::STAGES), (t / C::STAGES) & 1); };
-      // Issue order (ping-pong): tile A's P.V and its next Q.K^T go out as soon as softmax A hands P
-      // over, independently of tile B, so each softmax warpgroup overlaps the other tile's MMAs. The
-      // next S_g = Q_g K^T is issued right behind O_g += P_g V, although S_g's columns hold P_g: the
-      // tensor pipe executes one CTA's MMAs in issue order, so the P.V product has read P_g before the
-      // Q.K^T product writes there (the published FlashAttention-4 Blackwell kernel relies on the same
-      // ordering; the parity tests check the results bit for bit across reruns).
-      bool ok = wait(q_full(), 0) && kv_wait(0);
-      if (ok) {
-        tc_fence_after();
-        if (elect_one()) {
-          issue_qk(0, 0);
-          mma_commit(s_full(0));
-          if (has_b) {
-            issue_qk(1, 0);
-            mma_commit(s_full(1));
+      const int ng = has_b ? 2 : 1;
+      if (warp == MMA_WARP) {
+        // S_g = Q_g K^T: K-major operands, 16 of d per instruction.
+        auto issue_qk = [&](int g, int stage) {
+          const uint32_t a_off = (uint32_t)(g * C::Q_TILE) >> 4, b_off = (uint32_t)(stage * C::KV_TILE) >> 4;
+          const uint32_t d_t = tmem + (g ? C::T_S1 : C::T_S0);
+#pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint32_t oa = ((kk >> 2) * C::Q_SUB + (kk & 3) * 32) >> 4;
+            const uint32_t ob = ((kk >> 2) * C::KV_SUB + (kk & 3) * 32) >> 4;
+            mma_ss(d_t, dq + (a_off + oa), dk + (b_off + ob), idesc_qk, kk > 0 ? 1u : 0u);
           }
-          mma_commit(kv_empty(0));
-        }
-        __syncwarp();
-      }
-      for (int j = 0; ok && j < n_kv; ++j) {
-        const int tv = 2 * j + 1, tk = 2 * j + 2;  // positions of V_j and K_{j+1} in the load sequence
-        const int sv = tv % C::STAGES, sk = tk % C::STAGES;
-        const bool more = j + 1 < n_kv;
-        if (!(ok = kv_wait(tv))) break;
-        // ---- tile A: O_A += P_A V_j, then S_A = Q_A K_{j+1}^T
-        if (!(ok = wait(p_half(0), j & 1))) break;
-        tc_fence_after();
-        if (elect_one()) issue_pv(0, sv, j > 0, 0);
-        __syncwarp();
-        if (!(ok = wait(p_ready(0), j & 1))) break;
-        tc_fence_after();
-        if (elect_one()) {
-          issue_pv(0, sv, j > 0, 1);
-          mma_commit(o_done(0));
-        }
-        __syncwarp();
-        if (more) {
-          if (!(ok = kv_wait(tk))) break;
-          tc_fence_after();
-          if (elect_one()) {
-            issue_qk(0, sk);
-            mma_commit(s_full(0));
-          }
-          __syncwarp();
-        }
-        // ---- tile B
-        if (has_b) {
-          if (!(ok = wait(p_half(1), j & 1))) break;
-          tc_fence_after();
-          if (elect_one()) issue_pv(1, sv, j > 0, 0);
-          __syncwarp();
-          if (!(ok = wait(p_ready(1), j & 1))) break;
-          tc_fence_after();
-          if (elect_one()) {
-            issue_pv(1, sv, j > 0, 1);
-            mma_commit(o_done(1));
-            mma_commit(kv_empty(sv));
-          }
-          __syncwarp();
-          if (more) {
+        };
+        // Shared S region (d = 128): one sequence k = 0, 1, 2, ... of products, Q tile k % ng against
+        // K tile k / ng, product k issued once the softmax has read product k-1 (s_free).
+        // One S region per Q tile (d = 64): per K tile q, Q tile A then B, each once that tile's
+        // softmax has read its previous S.
+        bool ok = wait(q_full(), 0);
+        const int total = C::SHARED_S ? ng * n_kv : n_kv;
+        for (int k = 0; ok && k < total; ++k) {
+          const int q = C::SHARED_S ? k / ng : k;
+          const int g0 = C::SHARED_S ? k % ng : 0;
+          const int tk = 2 * q, sk = tk % C::STAGES;
+          if (g0 == 0 && !(ok = kv_wait(tk))) break;
+          for (int g = g0; g < (C::SHARED_S ? g0 + 1 : ng); ++g) {
+            if (k > 0 && !(ok = wait(s_free(C::SHARED_S ? 0 : g), (C::SHARED_S ? k - 1 : q - 1) & 1))) break;
+            tc_fence_after();
             if (elect_one()) {
-              issue_qk(1, sk);
-              mma_commit(s_full(1));
-              mma_commit(kv_empty(sk));
+              issue_qk(g, sk);
+              mma_commit(s_full(g));
+              if (g == ng - 1) mma_commit(kv_empty(sk));
             }
             __syncwarp();
           }
-        } else {
-          if (elect_one()) {
-            mma_commit(kv_empty(sv));
-            if (more) mma_commit(kv_empty(sk));
-          }
-          __syncwarp();
         }
+        if (elect_one()) mma_commit(drain_bar);
+        __syncwarp();
+        mbar_wait_drain(drain_bar, 0);
+      } else {
+        // O_g += P_g V: P from TMEM (8 columns per 16 keys), V as an MN-major operand, 16 keys per
+        // instruction; Q tile A then B for each V tile.
+        auto issue_pv = [&](int g, int stage, bool acc) {
+          const uint32_t b_off = (uint32_t)(stage * C::KV_TILE) >> 4;
+          const uint32_t d_t = tmem + (g ? C::T_O1 : C::T_O0);
+          const uint32_t p_t = tmem + (g ? C::T_P1 : C::T_P0);
+#pragma unroll
+          for (int kk = 0; kk < BN / 16; ++kk)
+            mma_ts(d_t, p_t + kk * 8, dv + (b_off + kk * (2048 >> 4)), idesc_pv, (acc || kk > 0) ? 1u : 0u);
+        };
+        bool ok = true;
+        for (int p = 0; ok && p < n_kv; ++p) {
+          const int tv = 2 * p + 1, sv = tv % C::STAGES;
+          if (!(ok = kv_wait(tv))) break;
+          for (int g = 0; g < ng; ++g) {
+            if (!(ok = wait(p_ready(g), p & 1))) break;
+            tc_fence_after();
+            if (elect_one()) {
+              issue_pv(g, sv, p > 0);
+              mma_commit(o_done(g));
+              if (g == ng - 1) mma_commit(kv_empty(sv));
+            }
+            __syncwarp();
+          }
+        }
+        if (elect_one()) mma_commit(drain_pv_bar);
+        __syncwarp();
+        mbar_wait_drain(drain_pv_bar, 0);
       }
-      // Drain: all MMAs issued by the elected lane complete before TMEM is released.
-      if (elect_one()) mma_commit(drain_bar);
-      __syncwarp();
-      mbar_wait_drain(drain_bar, 0);
     }
   } else {
-    // Softmax warpgroups.
+    // Softmax warpgroups: warps 0-3 own Q tile A, warps 4-7 Q tile B; thread t owns query row t =
+    // TMEM lane t, so the row max and row sum need no shuffles. Per K/V tile: load S, release the S
+    // columns, mask, take the max, wait for the previous P.V product (it reads P and writes O), rescale
+    // O only when the max grew by more than 2^8 (exact: every P and l of a row use the same reference
+    // max), write P = exp2(S*scale - m) as packed 16-bit pairs into the P columns, then arrive.
     setmaxnreg_inc<kRegsSoftmax>();
     const int g = warp >> 2;
     const int r_local = threadIdx.x & 127;  // row within the Q tile = TMEM lane
@@ -391,36 +386,41 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
       const int row = tile_row0 + r_local;
       const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
       const uint32_t t_s = tmem + lane_off + (g ? C::T_S1 : C::T_S0);
+      const uint32_t t_p = tmem + lane_off + (g ? C::T_P1 : C::T_P0);
       const uint32_t t_o = tmem + lane_off + (g ? C::T_O1 : C::T_O0);
       float m_used = -CUDART_INF_F, l = 0.f;
       bool ok = true;
       for (int j = 0; j < n_kv; ++j) {
-        ok = mbar_wait(s_full(g), j & 1, abort_flag, status, kErrSoftmaxWait);
-        ok = __all_sync(0xffffffffu, ok);
+        ok = __all_sync(0xffffffffu, mbar_wait(s_full(g), j & 1, abort_flag, status, kErrSoftmaxWait));
         if (!ok) break;
         tc_fence_after();
-        float s[128];
-        ld128(t_s, s);
+        float s[BN];
+        ld_row<BN>(t_s, s);
+        tc_fence_before();
+        mbar_arrive(s_free(C::SHARED_S ? 0 : g));  // the next Q.K^T may overwrite S now
         const int j0 = j * BN;
         if (j0 + BN > N || (causal && j0 + BN - 1 > tile_row0)) {
+          // columns c >= lim lie past N or (causal) after this row
+          const int lim = min(N, causal ? row + 1 : N) - j0;
 #pragma unroll
-          for (int c = 0; c < BN; ++c) {
-            const int col = j0 + c;
-            if (col >= N || (causal && col > row)) s[c] = -CUDART_INF_F;
-          }
+          for (int c = 0; c < BN; ++c) s[c] = c < lim ? s[c] : -CUDART_INF_F;
         }
-        const float m_new = row_max128(s) * scale_log2;
+        const float m_new = row_max<BN>(s) * scale_log2;
+        float alpha = 1.f;
+        bool need = false;
         if (j == 0) {
           m_used = m_new;
         } else {
-          const bool need = m_new > m_used + kRescaleThreshold;
+          need = m_new > m_used + kRescaleThreshold;
+          if (need) {
+            alpha = ex2(m_used - m_new);
+            m_used = m_new;
+          }
+          // O += P_{j-1} V_{j-1} must be complete: it reads the P columns and writes O.
+          ok = __all_sync(0xffffffffu, mbar_wait(o_done(g), (j - 1) & 1, abort_flag, status, kErrSoftmaxWait));
+          if (!ok) break;
+          tc_fence_after();
           if (__any_sync(0xffffffffu, need)) {
-            float alpha = 1.f;
-            if (need) {
-              alpha = ex2(m_used - m_new);
-              m_used = m_new;
-            }
-            l *= alpha;
 #pragma unroll
             for (int c = 0; c < D / 32; ++c) {
               uint32_t r[32];
@@ -432,30 +432,20 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
           }
         }
         const float m_sub = m_used == -CUDART_INF_F ? 0.f : m_used;
-        // P for keys 0-63 goes out first: the MMA warp starts the P.V product on it while keys 64-127
-        // are still being exponentiated; the row sum comes after both halves are handed over.
         uint32_t p[32];
-        if (pv_bf16)
-          softmax_half<true, 0>(s, scale_log2, m_sub, p);
-        else
-          softmax_half<false, 0>(s, scale_log2, m_sub, p);
-        tmem_st32(t_s, p);
-        tmem_wait_st();
-        tc_fence_before();
-        mbar_arrive(p_half(g));
-        if (pv_bf16)
-          softmax_half<true, 1>(s, scale_log2, m_sub, p);
-        else
-          softmax_half<false, 1>(s, scale_log2, m_sub, p);
-        tmem_st32(t_s + 32, p);
+        float psum = pv_bf16 ? softmax64<true, 0>(s, scale_log2, m_sub, p) : softmax64<false, 0>(s, scale_log2, m_sub, p);
+        tmem_st32(t_p, p);
+        if constexpr (BN == 128) {
+          psum += pv_bf16 ? softmax64<true, 64>(s, scale_log2, m_sub, p) : softmax64<false, 64>(s, scale_log2, m_sub, p);
+          tmem_st32(t_p + 32, p);
+        }
         tmem_wait_st();
         tc_fence_before();
         mbar_arrive(p_ready(g));
-        l += row_sum128(s);
+        l = l * alpha + psum;
       }
       if (ok) {
-        ok = mbar_wait(o_done(g), (n_kv - 1) & 1, abort_flag, status, kErrEpilogueWait);
-        ok = __all_sync(0xffffffffu, ok);
+        ok = __all_sync(0xffffffffu, mbar_wait(o_done(g), (n_kv - 1) & 1, abort_flag, status, kErrEpilogueWait));
       }
       if (ok) {
         tc_fence_after();
@@ -509,14 +499,14 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
-// (d, N, BH) view of a contiguous (BH, N, d) 16-bit array; 64 x 128 x 1 boxes, 128-byte swizzle.
+// (d, N, BH) view of a contiguous (BH, N, d) 16-bit array; 64 x rows x 1 boxes, 128-byte swizzle.
 // Rows past N read as zeros, per head.
-bool make_map(CUtensorMap* m, const void* base, int BH, int N, int d, bool bf16) {
+bool make_map(CUtensorMap* m, const void* base, int BH, int N, int d, bool bf16, int rows) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return false;
   const cuuint64_t dims[3] = {(cuuint64_t)d, (cuuint64_t)N, (cuuint64_t)BH};
   const cuuint64_t strides[2] = {(cuuint64_t)d * 2, (cuuint64_t)N * d * 2};
-  const cuuint32_t box[3] = {64, (cuuint32_t)tc::BM, 1};
+  const cuuint32_t box[3] = {64, (cuuint32_t)rows, 1};
   const cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = fn(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
                   const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
@@ -597,7 +587,7 @@ cudaError_t launch_d(const LaunchArgs& a, const CUtensorMap& mq, const CUtensorM
   note_launch();
   e = cudaGetLastError();
   CUtensorMap mvh;
-  if (e == cudaSuccess && !make_map(&mvh, vh, a.BH, a.N, D, false)) e = cudaErrorInvalidValue;
+  if (e == cudaSuccess && !make_map(&mvh, vh, a.BH, a.N, D, false, tc::Cfg<D>::BN)) e = cudaErrorInvalidValue;
   if (e == cudaSuccess) e = launch_t<D, true>(a, mq, mk, mv, mvh, flags);
   const cudaError_t ef = cudaFreeAsync(scratch, a.stream);
   return e != cudaSuccess ? e : ef;
@@ -617,7 +607,7 @@ cudaError_t launch_d_scratch(const LaunchArgs& a, const CUtensorMap& mq, const C
   note_launch();
   cudaError_t e = cudaGetLastError();
   CUtensorMap mvh;
-  if (e == cudaSuccess && !make_map(&mvh, vh, a.BH, a.N, D, false)) e = cudaErrorInvalidValue;
+  if (e == cudaSuccess && !make_map(&mvh, vh, a.BH, a.N, D, false, tc::Cfg<D>::BN)) e = cudaErrorInvalidValue;
   if (e == cudaSuccess) e = launch_t<D, true>(a, mq, mk, mv, mvh, flags);
   return e;
 }
@@ -633,18 +623,20 @@ size_t fused_tc_scratch_bytes(int BH, int N, int d, int dtype) {
 
 cudaError_t launch_fused_tc_sm100_scratch(const LaunchArgs& a, void* scratch) {
   const bool bf16 = a.dtype == PHANTOM_ATTN_BF16;
+  const int bn = a.d == 64 ? tc::Cfg<64>::BN : tc::Cfg<128>::BN;
   CUtensorMap mq, mk, mv;
-  if (!make_map(&mq, a.q, a.BH, a.N, a.d, bf16) || !make_map(&mk, a.k, a.BH, a.N, a.d, bf16) ||
-      !make_map(&mv, a.v, a.BH, a.N, a.d, bf16))
+  if (!make_map(&mq, a.q, a.BH, a.N, a.d, bf16, tc::BM) || !make_map(&mk, a.k, a.BH, a.N, a.d, bf16, bn) ||
+      !make_map(&mv, a.v, a.BH, a.N, a.d, bf16, bn))
     return cudaErrorInvalidValue;
   return a.d == 64 ? launch_d_scratch<64>(a, mq, mk, mv, scratch) : launch_d_scratch<128>(a, mq, mk, mv, scratch);
 }
 
 cudaError_t launch_fused_tc_sm100(const LaunchArgs& a) {
   const bool bf16 = a.dtype == PHANTOM_ATTN_BF16;
+  const int bn = a.d == 64 ? tc::Cfg<64>::BN : tc::Cfg<128>::BN;
   CUtensorMap mq, mk, mv;
-  if (!make_map(&mq, a.q, a.BH, a.N, a.d, bf16) || !make_map(&mk, a.k, a.BH, a.N, a.d, bf16) ||
-      !make_map(&mv, a.v, a.BH, a.N, a.d, bf16))
+  if (!make_map(&mq, a.q, a.BH, a.N, a.d, bf16, tc::BM) || !make_map(&mk, a.k, a.BH, a.N, a.d, bf16, bn) ||
+      !make_map(&mv, a.v, a.BH, a.N, a.d, bf16, bn))
     return cudaErrorInvalidValue;
   return a.d == 64 ? launch_d<64>(a, mq, mk, mv) : launch_d<128>(a, mq, mk, mv);
 }
