@@ -50,7 +50,9 @@ const char* phantom_attn_last_error(void);
 /*
  * v4 replacement: fused attention on 5th-generation tensor cores (tcgen05.mma, TMEM accumulators,
  * TMA-staged K/V ring). dtype PHANTOM_ATTN_F16 or PHANTOM_ATTN_BF16, head_dim 64 or 128, any
- * seq_len >= 1, causal 0/1. fp32 accumulation, P rounded to the input dtype for the P.V product.
+ * seq_len >= 1, causal 0/1. fp32 accumulation; P is rounded to fp16 for the P.V product (for bf16
+ * inputs V is staged as fp16 first; a head whose V holds a finite value beyond the fp16 range uses
+ * bf16 P and bf16 V instead).
  * Replaces attn::launch_fused_tc (reference csrc/kernels/fused_tc.cuh:187-196), which took
  * (const __half* q, k, v, __half* o, int BH, int N, bool causal, cudaStream_t) with d fixed at 64
  * and fp16 only; head_dim and dtype are explicit here because both are now selectable.
