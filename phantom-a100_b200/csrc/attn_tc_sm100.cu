@@ -13,6 +13,7 @@
 //
 // B200 mapping (not a translation of the WMMA kernel):
 //   * One CTA owns two 128-row Q tiles (A, B) of one (batch, head) and streams K/V tiles of 128 keys.
+//     CTAs are ordered heaviest first (causal) within groups of heads whose K/V fit in L2.
 //   * Warp 9 (one thread) is the TMA producer: Q tiles once, then K_0, V_0, K_1, V_1, ... into a ring
 //     of STAGES shared-memory slots (128-byte swizzle), completion tracked by mbarrier tx bytes.
 //   * Warp 8 (one thread) issues the S_g = Q_g K_j^T products (both operands in shared memory, fp32
@@ -37,6 +38,7 @@
 #include <cuda.h>
 #include <math_constants.h>
 
+#include <algorithm>
 #include <mutex>
 
 #include "launchers.h"
@@ -178,8 +180,8 @@ template <int D, bool BF16>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
 attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
             const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmVh,
-            const int* __restrict__ vflags, uint16_t* __restrict__ O, int N, float scale_log2, int causal,
-            int* __restrict__ status) {
+            const int* __restrict__ vflags, uint16_t* __restrict__ O, int BH, int N, float scale_log2, int causal,
+            int group_heads, int* __restrict__ status) {
   using C = Cfg<D>;
   constexpr int BN = C::BN;
   extern __shared__ uint8_t smem_raw[];
@@ -200,9 +202,16 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
   int* pv_bf16_flag = reinterpret_cast<int*>(smem + C::OFF_MISC + 8);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int bh = blockIdx.y;
+  // Block order (1-D grid, CTAs start roughly in index order): heads in groups of group_heads whose K
+  // and V fit in L2 together; inside a group, the query blocks of all its heads from the heaviest
+  // (causal: the most K/V tiles) to the lightest, so long CTAs start first and short ones fill the tail.
   const int n_qtiles = (N + BM - 1) / BM;
-  const int qblk = gridDim.x - 1 - blockIdx.x;  // heaviest (causal) blocks first
+  const int n_qblk = (n_qtiles + 1) / 2;
+  const int grp = blockIdx.x / (group_heads * n_qblk);
+  const int g_heads = min(group_heads, BH - grp * group_heads);
+  const int r_in = blockIdx.x - grp * group_heads * n_qblk;
+  const int bh = grp * group_heads + r_in % g_heads;
+  const int qblk = n_qblk - 1 - r_in / g_heads;
   const int qt0 = 2 * qblk;
   const bool has_b = qt0 + 1 < n_qtiles;
   const int row0 = qt0 * BM;
@@ -556,11 +565,16 @@ cudaError_t launch_t(const LaunchArgs& a, const CUtensorMap& mq, const CUtensorM
     attr_set[dev] = true;
   }
   const int n_qtiles = (a.N + tc::BM - 1) / tc::BM;
-  const dim3 grid((n_qtiles + 1) / 2, a.BH);
+  const int n_qblk = (n_qtiles + 1) / 2;
+  if ((long long)n_qblk * a.BH > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
+  const dim3 grid(n_qblk * a.BH);
+  // Heads per scheduling group: K and V of a group (4*N*d bytes per head) within ~48 MiB of L2.
+  const long long kv_bytes = 4LL * a.N * D;
+  const int group_heads = (int)std::max(1LL, std::min((long long)a.BH, (48LL << 20) / kv_bytes));
   const float scale_log2 = 1.4426950408889634f / sqrtf((float)D);
   timing_begin(a.stream);
-  kern<<<grid, tc::NUM_THREADS, smem, a.stream>>>(mq, mk, mv, mvh, vflags, static_cast<uint16_t*>(a.o), a.N,
-                                                   scale_log2, a.causal ? 1 : 0, a.status);
+  kern<<<grid, tc::NUM_THREADS, smem, a.stream>>>(mq, mk, mv, mvh, vflags, static_cast<uint16_t*>(a.o), a.BH, a.N,
+                                                   scale_log2, a.causal ? 1 : 0, group_heads, a.status);
   timing_end(a.stream);
   note_launch();
   return cudaGetLastError();

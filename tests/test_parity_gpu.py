@@ -79,6 +79,22 @@ def test_large_scores_do_not_overflow(capi, dtype, scale):
     assert np.abs(np64(o) - ref).max() < 1e-2 + 2.0 ** -7  # reference tolerance at this scale (+ bf16 ulp)
 
 
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("d", [64, 128])
+@pytest.mark.parametrize("causal", [False, True])
+@pytest.mark.parametrize("growth", [3.0, 10.0])
+def test_row_max_growing_mid_sequence(capi, dtype, d, causal, growth):
+    """Keys of the second half are `growth` times larger, so every row's running max jumps after the
+    first K/V tiles: the kernel must rescale O (accumulated by earlier P.V products) and l before the
+    next product, in whichever Q tile and TMEM region holds them."""
+    q, k, v = make_qkv(1, 2, 1500, d, dtype, seed=int(growth) * 7 + d)
+    k = k.clone()
+    k[:, :, 750:] = (k[:, :, 750:].float() * growth).to(dtype)
+    o = run_capi(capi, "fused_tc", q, k, v, causal)
+    ref = attention_naive(np64(q), np64(k), np64(v), causal)
+    assert_parity(np64(o), ref, torch_dtype_name(dtype), f"growth {growth} {dtype} d={d} causal={causal}")
+
+
 def test_bf16_head_beyond_fp16_range_falls_back_to_bf16_p(capi):
     """A bf16 V value outside the fp16 range makes that head compute P.V in bf16 (finite, looser bound);
     the other heads keep fp16 P and the tight bound."""
