@@ -119,6 +119,16 @@ int phantom_attn_tiled(const void* q, const void* k, const void* v, void* o, int
 int phantom_attn_device_status(int* status);
 
 /*
+ * Test support for the failure path: launches (asynchronously, on `stream`) a one-warp kernel that
+ * waits, with the same bounded mbarrier wait the attention kernels use, on a barrier that nothing
+ * arrives on. The wait gives up after its limit (about a second), and the kernel sets bit 16
+ * (PHANTOM_ATTN_STATUS_PROBE) of the device status word and exits; the context stays usable, and
+ * phantom_attn_device_status then reports and clears the bit. No counterpart in the reference.
+ */
+#define PHANTOM_ATTN_STATUS_PROBE 16
+int phantom_attn_wait_expiry_probe(void* stream);
+
+/*
  * Number of kernel launches made by this library on the calling thread since the last reset
  * (reset = 1 clears it). Used by the benchmark to count the launches in a timed region.
  */

@@ -486,6 +486,26 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
   }
 }
 
+// Failure-path probe: one warp waits, with the same bounded mbarrier wait the attention kernel uses,
+// on a barrier that nothing arrives on. The wait gives up after kWaitLimitCycles, raises the abort
+// flag and ORs kErrProbeWait into the status word; a second wait then returns at once on the flag.
+// Nothing is left in flight (no copies, no MMAs, no TMEM), so the context stays usable.
+constexpr int kErrProbeWait = 16;
+
+__global__ void __launch_bounds__(32, 1) wait_expiry_probe(int* __restrict__ status) {
+  __shared__ uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(smem_u32(&bar), 1);
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncwarp();
+  const bool first = mbar_wait(smem_u32(&bar), 0, &abort_flag, status, kErrProbeWait);
+  const bool second = mbar_wait(smem_u32(&bar), 0, &abort_flag, status, kErrProbeWait);
+  if (threadIdx.x == 0 && (first || second)) atomicOr(status, 1 << 30);  // a wait completed: impossible
+}
+
 }  // namespace tc
 
 // ------------------------------------------------------------------------------------ host side
@@ -653,6 +673,12 @@ cudaError_t launch_fused_tc_sm100(const LaunchArgs& a) {
       !make_map(&mv, a.v, a.BH, a.N, a.d, bf16, bn))
     return cudaErrorInvalidValue;
   return a.d == 64 ? launch_d<64>(a, mq, mk, mv) : launch_d<128>(a, mq, mk, mv);
+}
+
+cudaError_t launch_wait_expiry_probe(int* status, cudaStream_t stream) {
+  tc::wait_expiry_probe<<<1, 32, 0, stream>>>(status);
+  note_launch();
+  return cudaGetLastError();
 }
 
 }  // namespace phantom

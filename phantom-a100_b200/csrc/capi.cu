@@ -324,6 +324,16 @@ int phantom_attn_device_status(int* status) {
   return v == 0 ? PHANTOM_ATTN_OK : fail(PHANTOM_ATTN_ERR_DEVICE, "device status 0x%x: a bounded wait expired", v);
 }
 
+int phantom_attn_wait_expiry_probe(void* stream) {
+  Device dev;
+  int rc = current_device("wait_expiry_probe", &dev);
+  if (rc != PHANTOM_ATTN_OK) return rc;
+  const cudaError_t e = launch_wait_expiry_probe(dev.status, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail("wait_expiry_probe", e);
+  g_last_error.clear();
+  return PHANTOM_ATTN_OK;
+}
+
 int phantom_attn_kernel_timing(int enable) {
   g_timing.enabled = enable != 0;
   g_timing.used = 0;

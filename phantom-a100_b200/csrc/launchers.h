@@ -29,6 +29,9 @@ size_t fused_tc_scratch_bytes(int BH, int N, int d, int dtype);
 
 // CUDA-core fp32-arithmetic kernel. Any d in [1, 256], dtype F32/F16/BF16.
 cudaError_t launch_fused_simt(const LaunchArgs& a);
+// One-warp kernel whose bounded mbarrier wait must expire (nothing arrives on the barrier); sets bit 16
+// of *status (attn_tc_sm100.cu).
+cudaError_t launch_wait_expiry_probe(int* status, cudaStream_t stream);
 size_t fused_simt_smem_bytes(int d);
 
 // Number of kernel launches the library has made on this thread (benchmark accounting).

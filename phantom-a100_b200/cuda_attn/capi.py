@@ -30,6 +30,7 @@ SIGNATURES = {
     "phantom_attn_naive": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _I, _P]),
     "phantom_attn_tiled": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _I, _P]),
     "phantom_attn_device_status": (_I, [ctypes.POINTER(ctypes.c_int)]),
+    "phantom_attn_wait_expiry_probe": (_I, [_P]),
     "phantom_attn_launch_count": (ctypes.c_longlong, [_I]),
     "phantom_attn_kernel_timing": (_I, [_I]),
     "phantom_attn_kernel_timing_read": (_I, [ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_longlong)]),
@@ -118,6 +119,11 @@ class CAPI:
         if rc not in (OK, ERR_DEVICE):
             raise CapiError(rc, self.last_error())
         return st.value
+
+    def wait_expiry_probe(self, stream=None) -> None:
+        """Launch the kernel whose bounded wait must expire (about a second); device_status() then
+        reports STATUS_PROBE."""
+        self._check(self.lib.phantom_attn_wait_expiry_probe(self._stream(stream)))
 
     def launch_count(self, reset: bool = False) -> int:
         return int(self.lib.phantom_attn_launch_count(int(reset)))
