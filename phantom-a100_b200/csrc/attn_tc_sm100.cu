@@ -12,8 +12,11 @@
 // finite value beyond the fp16 range falls back to bf16 P and the original bf16 V for that head.
 //
 // B200 mapping (not a translation of the WMMA kernel):
-//   * One CTA owns two 128-row Q tiles (A, B) of one (batch, head) and streams K/V tiles of 128 keys.
-//     CTAs are ordered heaviest first (causal) within groups of heads whose K/V fit in L2.
+//   * Work unit: two 128-row Q tiles (A, B) of one (batch, head), streaming K/V tiles of 128 keys.
+//     Persistent CTAs (one per SM) take units one after another from an atomic counter, heaviest
+//     first (causal) within groups of heads whose K/V fit in L2; the K/V ring, the S sequence and all
+//     barrier phases run on across units, so the next unit's Q load and first S overlap the current
+//     unit's last tiles and output.
 //   * Warp 9 (one thread) is the TMA producer: Q tiles once, then K_0, V_0, K_1, V_1, ... into a ring
 //     of STAGES shared-memory slots (128-byte swizzle), completion tracked by mbarrier tx bytes.
 //   * Warp 8 (one thread) issues the S_g = Q_g K_j^T products (both operands in shared memory, fp32
@@ -62,6 +65,7 @@ constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale O only when th
 
 // Status-word bits (which wait expired).
 constexpr int kErrTmaWait = 1, kErrMmaWait = 2, kErrSoftmaxWait = 4, kErrEpilogueWait = 8;
+constexpr int kUnitRing = 4;  // published work-unit ids (shared memory)
 
 // TMEM plan per head dimension (K/V tiles of BN = 128 keys). P (the probabilities as packed 16-bit
 // pairs, the A operand of O += P V) never shares columns with S (fp32 scores), so a Q.K^T product is
@@ -85,10 +89,10 @@ struct Cfg {
   static constexpr int OFF_KV = 2 * Q_TILE;
   static constexpr int OFF_BAR = OFF_KV + STAGES * KV_TILE;
   // barriers: q_full, kv_full[STAGES], kv_empty[STAGES], s_full[2], s_free[2], p_ready[2], o_done[2],
-  // drain (S issuer), drain (P.V issuer)
-  static constexpr int NUM_BARS = 1 + 2 * STAGES + 10;
-  static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;  // TMEM base address, abort flag, P precision
-  static constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;  // + slack to align the base to 1024
+  // drain (S issuer), drain (P.V issuer), q_free, o_free[2]
+  static constexpr int NUM_BARS = 1 + 2 * STAGES + 13;
+  static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;  // TMEM base address, abort flag
+  static constexpr int SMEM_BYTES = OFF_MISC + 16 + 16 + 1024;  // + unit-id ring, + slack to align to 1024
   static constexpr uint32_t TMEM_COLS = 512;
   static constexpr uint32_t T_S0 = SHARED_S ? 0 : 2 * D, T_S1 = SHARED_S ? 0 : 2 * D + BN;
   static constexpr uint32_t T_P0 = SHARED_S ? BN : 2 * D + 2 * BN, T_P1 = T_P0 + BN / 2;
@@ -176,12 +180,15 @@ __device__ __forceinline__ float softmax64(const float (&s)[N], float scale_log2
 }
 
 // BF16: input/output dtype. vflags (bf16 only): per-(head, chunk) fp16-overflow flags of V.
+// Persistent: each CTA processes a sequence of work units (two 128-row Q tiles of one head); the K/V
+// ring, the S sequence and every barrier phase run on across units, so the next unit's Q is loaded and
+// its first S computed while the softmax warps still finish and write out the current unit.
 template <int D, bool BF16>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
 attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
             const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmVh,
             const int* __restrict__ vflags, uint16_t* __restrict__ O, int BH, int N, float scale_log2, int causal,
-            int group_heads, int* __restrict__ status) {
+            int group_heads, int* __restrict__ status, int* __restrict__ work_ctr) {
   using C = Cfg<D>;
   constexpr int BN = C::BN;
   extern __shared__ uint8_t smem_raw[];
@@ -197,26 +204,47 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
   auto o_done = [&](int g) { return bar0 + 8u * (7 + 2 * C::STAGES + g); };
   const uint32_t drain_bar = bar0 + 8u * (9 + 2 * C::STAGES);
   const uint32_t drain_pv_bar = bar0 + 8u * (10 + 2 * C::STAGES);
+  auto q_free = [&]() { return bar0 + 8u * (11 + 2 * C::STAGES); };
+  auto o_free = [&](int g) { return bar0 + 8u * (12 + 2 * C::STAGES + g); };
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 4);
-  int* pv_bf16_flag = reinterpret_cast<int*>(smem + C::OFF_MISC + 8);
+  volatile int* unit_ring = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 16);  // [kUnitRing]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // Block order (1-D grid, CTAs start roughly in index order): heads in groups of group_heads whose K
-  // and V fit in L2 together; inside a group, the query blocks of all its heads from the heaviest
-  // (causal: the most K/V tiles) to the lightest, so long CTAs start first and short ones fill the tail.
+  // Work units: (head, query block of two 128-row Q tiles). Unit order: heads in groups of group_heads
+  // whose K and V fit in L2 together; inside a group, the query blocks of all its heads from the
+  // heaviest (causal: the most K/V tiles) to the lightest. CTA c starts with unit c; each further unit
+  // is the next one in that order, taken with an atomic counter when the CTA is ready for it, so SMs
+  // that run faster take more units (list scheduling, longest first). The producer warp takes the
+  // units and publishes each id in a shared-memory ring before arriving on q_full; the other roles
+  // read it after their wait on q_full (they are at most one unit behind, so neither the phase nor the
+  // ring slot can be overtaken). An id of -1 ends every role's loop.
   const int n_qtiles = (N + BM - 1) / BM;
   const int n_qblk = (n_qtiles + 1) / 2;
-  const int grp = blockIdx.x / (group_heads * n_qblk);
-  const int g_heads = min(group_heads, BH - grp * group_heads);
-  const int r_in = blockIdx.x - grp * group_heads * n_qblk;
-  const int bh = grp * group_heads + r_in % g_heads;
-  const int qblk = n_qblk - 1 - r_in / g_heads;
-  const int qt0 = 2 * qblk;
-  const bool has_b = qt0 + 1 < n_qtiles;
-  const int row0 = qt0 * BM;
-  const int kv_end = causal ? min(N, row0 + (has_b ? 2 * BM : BM)) : N;
-  const int n_kv = (kv_end + BN - 1) / BN;
+  const int n_units = n_qblk * BH;
+  struct Unit {
+    int bh, row0, n_kv;
+    bool has_b;
+  };
+  auto unit_of = [&](int u) {
+    Unit x;
+    const int grp = u / (group_heads * n_qblk);
+    const int g_heads = min(group_heads, BH - grp * group_heads);
+    const int r_in = u - grp * group_heads * n_qblk;
+    x.bh = grp * group_heads + r_in % g_heads;
+    const int qt0 = 2 * (n_qblk - 1 - r_in / g_heads);
+    x.has_b = qt0 + 1 < n_qtiles;
+    x.row0 = qt0 * BM;
+    const int kv_end = causal ? min(N, x.row0 + (x.has_b ? 2 * BM : BM)) : N;
+    x.n_kv = (kv_end + BN - 1) / BN;
+    return x;
+  };
+  // P.V precision of a head (warp-wide: one flag per lane): fp16 unless a V value of the head
+  // overflows fp16 (bf16 inputs).
+  auto head_pv_bf16 = [&](int bh) -> bool {
+    if (!BF16) return false;
+    return __any_sync(0xffffffffu, vflags[bh * kVChunks + lane] != 0);
+  };
 
   if (threadIdx.x == 0) {
     mbar_init(q_full(), 1);
@@ -229,9 +257,11 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
       mbar_init(s_free(g), 128);
       mbar_init(p_ready(g), 128);
       mbar_init(o_done(g), 1);
+      mbar_init(o_free(g), 128);
     }
     mbar_init(drain_bar, 1);
     mbar_init(drain_pv_bar, 1);
+    mbar_init(q_free(), 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -239,57 +269,81 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
     tmem_alloc(smem_u32(tmem_holder), C::TMEM_COLS);
     tmem_relinquish();
   }
-  if (warp == MMA_WARP + 2) {
-    // P.V precision of this head: fp16 unless a V value of the head overflows fp16 (bf16 inputs).
-    int ovf = 0;
-    if (BF16) ovf = vflags[bh * kVChunks + lane] != 0;
-    ovf = __any_sync(0xffffffffu, ovf);
-    if (lane == 0) *pv_bf16_flag = ovf;
-  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
-  const bool pv_bf16 = BF16 && *pv_bf16_flag != 0;  // CTA-uniform
+
+  // Next unit id for a consumer role: wait for the unit's q_full phase, read the published id.
+  auto next_unit = [&](int nu, bool& ok) -> int {
+    ok = __all_sync(0xffffffffu, mbar_wait(q_full(), nu & 1, abort_flag, status, kErrMmaWait));
+    return ok ? unit_ring[nu % kUnitRing] : -1;
+  };
 
   if (warp == TMA_WARP || warp == PV_WARP + 1) {
     setmaxnreg_dec<kRegsProducer>();
     if (warp == TMA_WARP) {
-      // Producer: Q tiles once, then K_0, V_0, K_1, V_1, ... into the ring (warp-uniform loop, one
-      // elected lane issues the copies).
-      const CUtensorMap* tm_v = (BF16 && !pv_bf16) ? &tmVh : &tmV;
-      const int nq = has_b ? 2 : 1;
+      // Producer, per unit: take the unit, wait until the previous unit's last Q.K^T has read the Q
+      // buffer, publish the id, load the unit's Q tiles, then K_0, V_0, K_1, V_1, ... into the ring
+      // (warp-uniform loop, one elected lane issues copies).
+      int t = 0, nu = 0, nq_arrivals = 0;  // K/V copies, units issued, q_full phases started (+ end marker)
+      bool ok = true;
       if (elect_one()) {
         tma_prefetch_desc(&tmQ);
         tma_prefetch_desc(&tmK);
-        tma_prefetch_desc(tm_v);
-        mbar_arrive_expect_tx(q_full(), nq * C::Q_TILE);
-        for (int g = 0; g < nq; ++g)
-          for (int c = 0; c < C::KBLK; ++c)
-            tma_load_3d(sbase + C::OFF_Q + g * C::Q_TILE + c * C::Q_SUB, &tmQ, q_full(), c * 64, row0 + g * BM, bh);
+        tma_prefetch_desc(BF16 ? &tmVh : &tmV);
       }
       __syncwarp();
-      int issued = 0;
-      for (int t = 0; t < 2 * n_kv; ++t) {
-        const int s = t % C::STAGES, r = t / C::STAGES;
-        if (r > 0) {
-          const bool ok = __all_sync(0xffffffffu, mbar_wait(kv_empty(s), (r - 1) & 1, abort_flag, status, kErrTmaWait));
-          if (!ok) break;
+      for (;;) {
+        if (nu > 0 && !(ok = __all_sync(0xffffffffu, mbar_wait(q_free(), (nu - 1) & 1, abort_flag, status, kErrTmaWait))))
+          break;
+        int u = blockIdx.x;
+        if (nu > 0) {
+          int got = 0;
+          if (lane == 0) got = (int)gridDim.x + atomicAdd(work_ctr, 1);
+          u = __shfl_sync(0xffffffffu, got, 0);
         }
-        const CUtensorMap* m = (t & 1) ? tm_v : &tmK;
-        const int j = t >> 1;
+        if (u >= n_units) u = -1;
+        if (u < 0) {
+          if (elect_one()) {
+            unit_ring[nu % kUnitRing] = -1;
+            mbar_arrive(q_full());  // release semantics: the consumers' wait sees the id
+          }
+          __syncwarp();
+          ++nq_arrivals;
+          break;
+        }
+        const Unit x = unit_of(u);
+        const CUtensorMap* tm_v = (BF16 && !head_pv_bf16(x.bh)) ? &tmVh : &tmV;
+        const int nq = x.has_b ? 2 : 1;
         if (elect_one()) {
-          mbar_arrive_expect_tx(kv_full(s), C::KV_TILE);
-          for (int c = 0; c < C::KBLK; ++c)
-            tma_load_3d(sbase + C::OFF_KV + s * C::KV_TILE + c * C::KV_SUB, m, kv_full(s), c * 64, j * BN, bh);
+          unit_ring[nu % kUnitRing] = u;
+          mbar_arrive_expect_tx(q_full(), nq * C::Q_TILE);
+          for (int g = 0; g < nq; ++g)
+            for (int c = 0; c < C::KBLK; ++c)
+              tma_load_3d(sbase + C::OFF_Q + g * C::Q_TILE + c * C::Q_SUB, &tmQ, q_full(), c * 64, x.row0 + g * BM, x.bh);
         }
         __syncwarp();
-        issued = t + 1;
+        ++nu;
+        ++nq_arrivals;
+        for (int jt = 0; jt < 2 * x.n_kv; ++jt, ++t) {
+          const int s = t % C::STAGES, rr = t / C::STAGES;
+          if (rr > 0 && !(ok = __all_sync(0xffffffffu, mbar_wait(kv_empty(s), (rr - 1) & 1, abort_flag, status, kErrTmaWait))))
+            break;
+          const CUtensorMap* m = (jt & 1) ? tm_v : &tmK;
+          if (elect_one()) {
+            mbar_arrive_expect_tx(kv_full(s), C::KV_TILE);
+            for (int c = 0; c < C::KBLK; ++c)
+              tma_load_3d(sbase + C::OFF_KV + s * C::KV_TILE + c * C::KV_SUB, m, kv_full(s), c * 64, (jt >> 1) * BN, x.bh);
+          }
+          __syncwarp();
+        }
       }
       // Drain: every issued copy must land before this CTA's shared memory can be released.
-      mbar_wait_drain(q_full(), 0);
-      for (int t = (issued > C::STAGES ? issued - C::STAGES : 0); t < issued; ++t)
-        mbar_wait_drain(kv_full(t % C::STAGES), (t / C::STAGES) & 1);
+      // (phases complete in order: the last q_full phase started covers every Q copy)
+      if (nq_arrivals > 0) mbar_wait_drain(q_full(), (nq_arrivals - 1) & 1);
+      if (!ok) *abort_flag = 1;  // consumers waiting for a unit id stop at once
+      for (int i = (t > C::STAGES ? t - C::STAGES : 0); i < t; ++i) mbar_wait_drain(kv_full(i % C::STAGES), (i / C::STAGES) & 1);
     }
   } else if (warp == MMA_WARP || warp == PV_WARP) {
     setmaxnreg_dec<kRegsProducer>();
@@ -301,7 +355,6 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
     // the softmax warps and the barriers below.
     {
       constexpr uint32_t idesc_qk = idesc_f16(BF16, BM, BN, false);
-      const uint32_t idesc_pv = idesc_f16(pv_bf16, BM, D, true);
       // Descriptors are formed as (region base descriptor) + (byte offset >> 4): the start-address
       // field is the low 14 bits and every operand lies below 256 KB of shared memory, so the addition
       // never carries out of the field.
@@ -312,7 +365,6 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
         return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag, status, kErrMmaWait));
       };
       auto kv_wait = [&](int t) { return wait(kv_full(t % C::STAGES), (t / C::STAGES) & 1); };
-      const int ng = has_b ? 2 : 1;
       if (warp == MMA_WARP) {
         // S_g = Q_g K^T: K-major operands, 16 of d per instruction.
         auto issue_qk = [&](int g, int stage) {
@@ -325,56 +377,87 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
             mma_ss(d_t, dq + (a_off + oa), dk + (b_off + ob), idesc_qk, kk > 0 ? 1u : 0u);
           }
         };
-        // Shared S region (d = 128): one sequence k = 0, 1, 2, ... of products, Q tile k % ng against
-        // K tile k / ng, product k issued once the softmax has read product k-1 (s_free).
-        // One S region per Q tile (d = 64): per K tile q, Q tile A then B, each once that tile's
-        // softmax has read its previous S.
-        bool ok = wait(q_full(), 0);
-        const int total = C::SHARED_S ? ng * n_kv : n_kv;
-        for (int k = 0; ok && k < total; ++k) {
-          const int q = C::SHARED_S ? k / ng : k;
-          const int g0 = C::SHARED_S ? k % ng : 0;
-          const int tk = 2 * q, sk = tk % C::STAGES;
-          if (g0 == 0 && !(ok = kv_wait(tk))) break;
-          for (int g = g0; g < (C::SHARED_S ? g0 + 1 : ng); ++g) {
-            if (k > 0 && !(ok = wait(s_free(C::SHARED_S ? 0 : g), (C::SHARED_S ? k - 1 : q - 1) & 1))) break;
-            tc_fence_after();
-            if (elect_one()) {
-              issue_qk(g, sk);
-              mma_commit(s_full(g));
-              if (g == ng - 1) mma_commit(kv_empty(sk));
+        // Shared S region (d = 128): one sequence of products over all units, in a unit Q tile k % ng
+        // against K tile k / ng; each product is issued once the softmax has read the previous one
+        // (s_free). One S region per Q tile (d = 64): per K tile, Q tile A then B, each once that tile's
+        // softmax has read its previous S. After a unit's last product, q_free lets the producer load
+        // the next unit's Q.
+        int tb = 0, nu = 0, ks = 0;  // first K/V copy of the unit, units done, S products (shared S)
+        int qc[2] = {0, 0};          // S products per Q tile (separate S)
+        bool ok = true;
+        for (;;) {
+          const int u = next_unit(nu, ok);
+          if (u < 0) break;
+          const Unit x = unit_of(u);
+          const int ng = x.has_b ? 2 : 1;
+          const int total = C::SHARED_S ? ng * x.n_kv : x.n_kv;
+          for (int k = 0; ok && k < total; ++k) {
+            const int q = C::SHARED_S ? k / ng : k;
+            const int g0 = C::SHARED_S ? k % ng : 0;
+            const int tk = tb + 2 * q, sk = tk % C::STAGES;
+            if (g0 == 0 && !(ok = kv_wait(tk))) break;
+            for (int g = g0; g < (C::SHARED_S ? g0 + 1 : ng); ++g) {
+              const int n_prev = C::SHARED_S ? ks : qc[g];
+              if (n_prev > 0 && !(ok = wait(s_free(C::SHARED_S ? 0 : g), (n_prev - 1) & 1))) break;
+              tc_fence_after();
+              if (elect_one()) {
+                issue_qk(g, sk);
+                mma_commit(s_full(g));
+                if (g == ng - 1) mma_commit(kv_empty(sk));
+              }
+              __syncwarp();
+              if (C::SHARED_S) ++ks; else ++qc[g];
             }
-            __syncwarp();
           }
+          if (!ok) break;
+          if (elect_one()) mma_commit(q_free());
+          __syncwarp();
+          tb += 2 * x.n_kv;
+          ++nu;
         }
         if (elect_one()) mma_commit(drain_bar);
         __syncwarp();
         mbar_wait_drain(drain_bar, 0);
       } else {
         // O_g += P_g V: P from TMEM (8 columns per 16 keys), V as an MN-major operand, 16 keys per
-        // instruction; Q tile A then B for each V tile.
-        auto issue_pv = [&](int g, int stage, bool acc) {
-          const uint32_t b_off = (uint32_t)(stage * C::KV_TILE) >> 4;
-          const uint32_t d_t = tmem + (g ? C::T_O1 : C::T_O0);
-          const uint32_t p_t = tmem + (g ? C::T_P1 : C::T_P0);
-#pragma unroll
-          for (int kk = 0; kk < BN / 16; ++kk)
-            mma_ts(d_t, p_t + kk * 8, dv + (b_off + kk * (2048 >> 4)), idesc_pv, (acc || kk > 0) ? 1u : 0u);
-        };
+        // instruction; Q tile A then B for each V tile. A unit's first product overwrites O_g, so it
+        // waits until the softmax has read the previous unit's O_g out (o_free).
+        int tb = 0, nu = 0;
+        int pc[2] = {0, 0}, uc[2] = {0, 0};  // P.V products and units per Q tile
         bool ok = true;
-        for (int p = 0; ok && p < n_kv; ++p) {
-          const int tv = 2 * p + 1, sv = tv % C::STAGES;
-          if (!(ok = kv_wait(tv))) break;
-          for (int g = 0; g < ng; ++g) {
-            if (!(ok = wait(p_ready(g), p & 1))) break;
-            tc_fence_after();
-            if (elect_one()) {
-              issue_pv(g, sv, p > 0);
-              mma_commit(o_done(g));
-              if (g == ng - 1) mma_commit(kv_empty(sv));
+        for (;; ++nu) {
+          const int u = next_unit(nu, ok);
+          if (u < 0) break;
+          const Unit x = unit_of(u);
+          const int ng = x.has_b ? 2 : 1;
+          const uint32_t idesc_pv = idesc_f16(head_pv_bf16(x.bh), BM, D, true);
+          auto issue_pv = [&](int g, int stage, bool acc) {
+            const uint32_t b_off = (uint32_t)(stage * C::KV_TILE) >> 4;
+            const uint32_t d_t = tmem + (g ? C::T_O1 : C::T_O0);
+            const uint32_t p_t = tmem + (g ? C::T_P1 : C::T_P0);
+#pragma unroll
+            for (int kk = 0; kk < BN / 16; ++kk)
+              mma_ts(d_t, p_t + kk * 8, dv + (b_off + kk * (2048 >> 4)), idesc_pv, (acc || kk > 0) ? 1u : 0u);
+          };
+          for (int p = 0; ok && p < x.n_kv; ++p) {
+            const int tv = tb + 2 * p + 1, sv = tv % C::STAGES;
+            if (!(ok = kv_wait(tv))) break;
+            for (int g = 0; g < ng; ++g) {
+              if (p == 0 && uc[g] > 0 && !(ok = wait(o_free(g), (uc[g] - 1) & 1))) break;
+              if (!(ok = wait(p_ready(g), pc[g] & 1))) break;
+              tc_fence_after();
+              if (elect_one()) {
+                issue_pv(g, sv, p > 0);
+                mma_commit(o_done(g));
+                if (g == ng - 1) mma_commit(kv_empty(sv));
+              }
+              __syncwarp();
+              ++pc[g];
             }
-            __syncwarp();
           }
+          if (!ok) break;
+          for (int g = 0; g < ng; ++g) ++uc[g];
+          tb += 2 * x.n_kv;
         }
         if (elect_one()) mma_commit(drain_pv_bar);
         __syncwarp();
@@ -382,26 +465,35 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
       }
     }
   } else {
-    // Softmax warpgroups: warps 0-3 own Q tile A, warps 4-7 Q tile B; thread t owns query row t =
-    // TMEM lane t, so the row max and row sum need no shuffles. Per K/V tile: load S, release the S
-    // columns, mask, take the max, wait for the previous P.V product (it reads P and writes O), rescale
-    // O only when the max grew by more than 2^8 (exact: every P and l of a row use the same reference
-    // max), write P = exp2(S*scale - m) as packed 16-bit pairs into the P columns, then arrive.
+    // Softmax warpgroups: warps 0-3 own Q tile A, warps 4-7 Q tile B of every unit; thread t owns
+    // query row t = TMEM lane t, so the row max and row sum need no shuffles. Per K/V tile: load S,
+    // release the S columns, mask, take the max, wait for the previous P.V product (it reads P and
+    // writes O), rescale O only when the max grew by more than 2^8 (exact: every P and l of a row use
+    // the same reference max), write P = exp2(S*scale - m) as packed 16-bit pairs into the P columns,
+    // then arrive. After a unit's last tile: O / l to global memory, then release O (o_free).
     setmaxnreg_inc<kRegsSoftmax>();
     const int g = warp >> 2;
     const int r_local = threadIdx.x & 127;  // row within the Q tile = TMEM lane
-    if (g == 0 || has_b) {
-      const int tile_row0 = row0 + g * BM;
+    const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
+    const uint32_t t_s = tmem + lane_off + (g ? C::T_S1 : C::T_S0);
+    const uint32_t t_p = tmem + lane_off + (g ? C::T_P1 : C::T_P0);
+    const uint32_t t_o = tmem + lane_off + (g ? C::T_O1 : C::T_O0);
+    int sc = 0, oc = 0;  // S products read and P.V products waited for, this Q tile, all units
+    bool ok = true;
+    for (int nu = 0;; ++nu) {
+      const int u = next_unit(nu, ok);
+      if (u < 0) break;
+      const Unit x = unit_of(u);
+      if (g == 1 && !x.has_b) continue;
+      const bool pv_bf16 = head_pv_bf16(x.bh);
+      const int n_kv = x.n_kv;
+      const int tile_row0 = x.row0 + g * BM;
       const int row = tile_row0 + r_local;
-      const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
-      const uint32_t t_s = tmem + lane_off + (g ? C::T_S1 : C::T_S0);
-      const uint32_t t_p = tmem + lane_off + (g ? C::T_P1 : C::T_P0);
-      const uint32_t t_o = tmem + lane_off + (g ? C::T_O1 : C::T_O0);
       float m_used = -CUDART_INF_F, l = 0.f;
-      bool ok = true;
       for (int j = 0; j < n_kv; ++j) {
-        ok = __all_sync(0xffffffffu, mbar_wait(s_full(g), j & 1, abort_flag, status, kErrSoftmaxWait));
+        ok = __all_sync(0xffffffffu, mbar_wait(s_full(g), sc & 1, abort_flag, status, kErrSoftmaxWait));
         if (!ok) break;
+        ++sc;
         tc_fence_after();
         float s[BN];
         ld_row<BN>(t_s, s);
@@ -426,17 +518,18 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
             m_used = m_new;
           }
           // O += P_{j-1} V_{j-1} must be complete: it reads the P columns and writes O.
-          ok = __all_sync(0xffffffffu, mbar_wait(o_done(g), (j - 1) & 1, abort_flag, status, kErrSoftmaxWait));
+          ok = __all_sync(0xffffffffu, mbar_wait(o_done(g), oc & 1, abort_flag, status, kErrSoftmaxWait));
           if (!ok) break;
+          ++oc;
           tc_fence_after();
           if (__any_sync(0xffffffffu, need)) {
 #pragma unroll
             for (int c = 0; c < D / 32; ++c) {
-              uint32_t r[32];
-              tmem_ld32_wait(t_o + c * 32, r);
+              uint32_t rr[32];
+              tmem_ld32_wait(t_o + c * 32, rr);
 #pragma unroll
-              for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
-              tmem_st32(t_o + c * 32, r);
+              for (int i = 0; i < 32; ++i) rr[i] = __float_as_uint(__uint_as_float(rr[i]) * alpha);
+              tmem_st32(t_o + c * 32, rr);
             }
           }
         }
@@ -453,28 +546,29 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
         mbar_arrive(p_ready(g));
         l = l * alpha + psum;
       }
-      if (ok) {
-        ok = __all_sync(0xffffffffu, mbar_wait(o_done(g), (n_kv - 1) & 1, abort_flag, status, kErrEpilogueWait));
-      }
-      if (ok) {
-        tc_fence_after();
-        const float inv_l = 1.f / l;
-        uint16_t* out = O + ((size_t)bh * N + row) * D;
+      if (!ok) break;
+      ok = __all_sync(0xffffffffu, mbar_wait(o_done(g), oc & 1, abort_flag, status, kErrEpilogueWait));
+      if (!ok) break;
+      ++oc;
+      tc_fence_after();
+      const float inv_l = 1.f / l;
+      uint16_t* out = O + ((size_t)x.bh * N + row) * D;
 #pragma unroll
-        for (int c = 0; c < D / 32; ++c) {
-          uint32_t r[32];
-          tmem_ld32_wait(t_o + c * 32, r);
-          uint32_t w[16];
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t rr[32];
+        tmem_ld32_wait(t_o + c * 32, rr);
+        uint32_t w[16];
 #pragma unroll
-          for (int i = 0; i < 16; ++i)
-            w[i] = pack2<BF16>(__uint_as_float(r[2 * i]) * inv_l, __uint_as_float(r[2 * i + 1]) * inv_l);
-          if (row < N) {
-            uint4* dst = reinterpret_cast<uint4*>(out + c * 32);
+        for (int i = 0; i < 16; ++i)
+          w[i] = pack2<BF16>(__uint_as_float(rr[2 * i]) * inv_l, __uint_as_float(rr[2 * i + 1]) * inv_l);
+        if (row < N) {
+          uint4* dst = reinterpret_cast<uint4*>(out + c * 32);
 #pragma unroll
-            for (int i = 0; i < 4; ++i) dst[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
-          }
+          for (int i = 0; i < 4; ++i) dst[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
         }
       }
+      tc_fence_before();
+      mbar_arrive(o_free(g));  // the next unit's first P.V may overwrite O now
     }
   }
 
@@ -587,14 +681,25 @@ cudaError_t launch_t(const LaunchArgs& a, const CUtensorMap& mq, const CUtensorM
   const int n_qtiles = (a.N + tc::BM - 1) / tc::BM;
   const int n_qblk = (n_qtiles + 1) / 2;
   if ((long long)n_qblk * a.BH > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
-  const dim3 grid(n_qblk * a.BH);
+  // Persistent grid: one CTA per SM (at most one per work unit).
+  static int sm_count[kMaxDevices] = {};
+  if (dev < kMaxDevices && sm_count[dev] == 0) {
+    cudaError_t e = cudaDeviceGetAttribute(&sm_count[dev], cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return e;
+  }
+  const int n_sm = dev < kMaxDevices ? sm_count[dev] : 148;
+  const dim3 grid((unsigned)std::min<long long>((long long)n_qblk * a.BH, n_sm));
   // Heads per scheduling group: K and V of a group (4*N*d bytes per head) within ~48 MiB of L2.
   const long long kv_bytes = 4LL * a.N * D;
   const int group_heads = (int)std::max(1LL, std::min((long long)a.BH, (48LL << 20) / kv_bytes));
   const float scale_log2 = 1.4426950408889634f / sqrtf((float)D);
+  // Work counter of the persistent CTAs: the int 128 bytes into the (256-byte) status allocation.
+  int* work_ctr = a.status + 32;
+  cudaError_t e0 = cudaMemsetAsync(work_ctr, 0, sizeof(int), a.stream);
+  if (e0 != cudaSuccess) return e0;
   timing_begin(a.stream);
   kern<<<grid, tc::NUM_THREADS, smem, a.stream>>>(mq, mk, mv, mvh, vflags, static_cast<uint16_t*>(a.o), a.BH, a.N,
-                                                   scale_log2, a.causal ? 1 : 0, group_heads, a.status);
+                                                   scale_log2, a.causal ? 1 : 0, group_heads, a.status, work_ctr);
   timing_end(a.stream);
   note_launch();
   return cudaGetLastError();

@@ -55,7 +55,8 @@ struct Device {
   int* status = nullptr;
 };
 
-// Current device, its properties and its status word (allocated once per device, zeroed).
+// Current device, its properties and its 256-byte status region (allocated once per device, zeroed):
+// the status word at byte 0, the tensor-core kernel's work counter at byte 128.
 int current_device(const char* name, Device* out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -160,9 +161,10 @@ int simt_entry(const char* name, const void* q, const void* k, const void* v, vo
 }
 
 // ------------------------------------------------------------------ entry point without allocation
-// Scratch of phantom_attn_fused_tc_noalloc, laid out as [status word (256 B) | fp16 copy of V |
-// V overflow flags]. A file-scope device array: every GPU that loads this library holds these 64 MiB
-// until the process exits. All calls on a device share it.
+// Scratch of phantom_attn_fused_tc_noalloc, laid out as [status region (256 B: status word; the
+// persistent CTAs' work counter at byte 128) | fp16 copy of V | V overflow flags]. A file-scope device
+// array: every GPU that loads this library holds these 64 MiB until the process exits. All calls on a
+// device share it.
 constexpr size_t kNoAllocScratchBytes = size_t(64) << 20;
 constexpr size_t kNoAllocStatusBytes = 256;
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
