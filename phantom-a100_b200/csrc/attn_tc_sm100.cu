@@ -691,7 +691,7 @@ cudaError_t launch_t(const LaunchArgs& a, const CUtensorMap& mq, const CUtensorM
   const dim3 grid((unsigned)std::min<long long>((long long)n_qblk * a.BH, n_sm));
   // Heads per scheduling group: K and V of a group (4*N*d bytes per head) within ~16 MiB of L2. The
   // persistent CTAs drift apart in their K/V streams, so a group's whole K/V is live in L2 at once; with
-  // 48 MiB groups config 4 re-read 1.7x its K/V from DRAM, with 16 MiB none (ncu), at equal speed.
+  // 48 MiB groups config 4 read its K/V 2-2.3x from DRAM, with 16 MiB once (ncu), at equal speed.
   const long long kv_bytes = 4LL * a.N * D;
   const int group_heads = (int)std::max(1LL, std::min((long long)a.BH, (16LL << 20) / kv_bytes));
   const float scale_log2 = 1.4426950408889634f / sqrtf((float)D);
