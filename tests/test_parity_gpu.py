@@ -108,6 +108,35 @@ def test_bf16_head_beyond_fp16_range_falls_back_to_bf16_p(capi):
     assert rel < 5e-3, rel
 
 
+@pytest.mark.parametrize("d", [64, 128])
+@pytest.mark.parametrize("causal", [False, True])
+def test_persistent_ctas_mixed_units(capi, d, causal):
+    """160 heads at N = 300: 320 work units (a two-tile and a one-tile query block per head) on at most
+    one persistent CTA per SM, so every CTA runs several units of both shapes back to back and its
+    barrier phases, K/V ring and TMEM regions carry across unit boundaries."""
+    q, k, v = make_qkv(2, 80, 300, d, torch.float16, seed=11 + d)
+    o = run_capi(capi, "fused_tc", q, k, v, causal)
+    ref = attention_naive(np64(q), np64(k), np64(v), causal)
+    assert_parity(np64(o), ref, "float16", f"160 heads d={d} causal={causal}")
+
+
+def test_bf16_fallback_heads_among_fp16_p_heads(capi):
+    """Every seventh of 160 bf16 heads holds a V value beyond the fp16 range: persistent CTAs switch
+    between fp16 P (fp16-staged V) and bf16 P (original V) from one unit to the next."""
+    q, k, v = make_qkv(1, 160, 300, 128, torch.bfloat16, seed=21)
+    bad = list(range(0, 160, 7))
+    for h in bad:
+        v[0, h, (h * 13) % 300, h % 128] = 1.0e6
+    o = run_capi(capi, "fused_tc", q, k, v)
+    assert torch.isfinite(o).all()
+    ref = attention_naive(np64(q), np64(k), np64(v))
+    good = [h for h in range(160) if h not in bad]
+    assert_parity(np64(o)[:, good], ref[:, good], "bfloat16", "fp16-P heads")
+    for h in bad:
+        rel = np.linalg.norm(np64(o)[:, h] - ref[:, h]) / np.linalg.norm(ref[:, h])
+        assert rel < 5e-3, (h, rel)
+
+
 def test_non_default_stream(capi):
     q, k, v = make_qkv(1, 4, 777, 128, torch.bfloat16, seed=3)
     s = torch.cuda.Stream()
