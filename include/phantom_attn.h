@@ -145,6 +145,22 @@ long long phantom_attn_launch_count(int reset);
 int phantom_attn_kernel_timing(int enable);
 int phantom_attn_kernel_timing_read(double* total_ms, long long* launches);
 
+/*
+ * Launch-shape override of the tensor-core kernel (fused_tc, fused_tuned, fused_tc_noalloc) for the
+ * calling thread; the tile sweep's knobs. No counterpart in the reference: its tuning knobs were the
+ * compiled (br, bc) tiles and double buffering (reference bench/sweep_tiles.py:22-63), which on sm_100a
+ * are fixed by the tcgen05 instruction shape. 0 selects the automatic value.
+ *   l2_group_kib  K and V bytes (4 * N * head_dim per head) of one scheduling group of heads, in KiB;
+ *                 the persistent CTAs take all query blocks of a group before the next group, so a group
+ *                 within L2 streams its K/V from DRAM once. Automatic: 16384 (16 MiB). At least one head.
+ *   max_ctas      cap on the persistent grid (automatic: one CTA per SM), e.g. to leave SMs to work on
+ *                 another stream.
+ * Results do not depend on either value. Returns PHANTOM_ATTN_ERR_INVALID for a negative value or
+ * l2_group_kib above 2^40.
+ */
+int phantom_attn_set_launch_shape(long long l2_group_kib, int max_ctas);
+int phantom_attn_get_launch_shape(long long* l2_group_kib, int* max_ctas);
+
 #ifdef __cplusplus
 }
 #endif

@@ -298,7 +298,9 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
         if (nu > 0 && !(ok = __all_sync(0xffffffffu, mbar_wait(q_free(), (nu - 1) & 1, abort_flag, status, kErrTmaWait))))
           break;
         int u = blockIdx.x;
-        if (nu > 0) {
+        if (nu > 0 && n_units <= (int)gridDim.x) {
+          u = n_units;  // one wave: every unit was some CTA's first, the counter is not used
+        } else if (nu > 0) {
           int got = 0;
           if (lane == 0) got = (int)gridDim.x + atomicAdd(work_ctr, 1);
           u = __shfl_sync(0xffffffffu, got, 0);
@@ -687,18 +689,24 @@ cudaError_t launch_t(const LaunchArgs& a, const CUtensorMap& mq, const CUtensorM
     cudaError_t e = cudaDeviceGetAttribute(&sm_count[dev], cudaDevAttrMultiProcessorCount, dev);
     if (e != cudaSuccess) return e;
   }
-  const int n_sm = dev < kMaxDevices ? sm_count[dev] : 148;
+  const LaunchShape& shape = launch_shape();
+  int n_sm = dev < kMaxDevices ? sm_count[dev] : 148;
+  if (shape.max_ctas > 0) n_sm = std::min(n_sm, shape.max_ctas);
   const dim3 grid((unsigned)std::min<long long>((long long)n_qblk * a.BH, n_sm));
   // Heads per scheduling group: K and V of a group (4*N*d bytes per head) within ~16 MiB of L2. The
   // persistent CTAs drift apart in their K/V streams, so a group's whole K/V is live in L2 at once; with
   // 48 MiB groups config 4 read its K/V 2-2.3x from DRAM, with 16 MiB once (ncu), at equal speed.
   const long long kv_bytes = 4LL * a.N * D;
-  const int group_heads = (int)std::max(1LL, std::min((long long)a.BH, (16LL << 20) / kv_bytes));
+  const long long group_bytes = shape.l2_group_kib > 0 ? shape.l2_group_kib << 10 : 16LL << 20;
+  const int group_heads = (int)std::max(1LL, std::min((long long)a.BH, group_bytes / kv_bytes));
   const float scale_log2 = 1.4426950408889634f / sqrtf((float)D);
-  // Work counter of the persistent CTAs: the int 128 bytes into the (256-byte) status allocation.
+  // Work counter of the persistent CTAs: the int 128 bytes into the (256-byte) status allocation. A
+  // launch of one wave (units <= CTAs) never reads it, so only larger launches reset it.
   int* work_ctr = a.status + 32;
-  cudaError_t e0 = cudaMemsetAsync(work_ctr, 0, sizeof(int), a.stream);
-  if (e0 != cudaSuccess) return e0;
+  if ((long long)n_qblk * a.BH > (long long)grid.x) {
+    cudaError_t e0 = cudaMemsetAsync(work_ctr, 0, sizeof(int), a.stream);
+    if (e0 != cudaSuccess) return e0;
+  }
   timing_begin(a.stream);
   kern<<<grid, tc::NUM_THREADS, smem, a.stream>>>(mq, mk, mv, mvh, vflags, static_cast<uint16_t*>(a.o), a.BH, a.N,
                                                    scale_log2, a.causal ? 1 : 0, group_heads, a.status, work_ctr);

@@ -27,6 +27,7 @@ struct Timing {
   int device = -1;
 };
 thread_local Timing g_timing;
+thread_local LaunchShape g_shape;
 
 int fail(int code, const char* fmt, ...) {
   char buf[512];
@@ -203,6 +204,8 @@ int noalloc_setup(const char* name, int dev, unsigned char** scratch, int* cc, i
 
 void note_launch() { ++g_launches; }
 
+const LaunchShape& launch_shape() { return g_shape; }
+
 void timing_begin(cudaStream_t s) {
   Timing& t = g_timing;
   if (!t.enabled) return;
@@ -355,6 +358,23 @@ int phantom_attn_kernel_timing_read(double* total_ms, long long* launches) {
   }
   *total_ms = sum;
   *launches = (long long)g_timing.used;
+  return PHANTOM_ATTN_OK;
+}
+
+int phantom_attn_set_launch_shape(long long l2_group_kib, int max_ctas) {
+  if (l2_group_kib < 0 || l2_group_kib > (1LL << 40) || max_ctas < 0)
+    return fail(PHANTOM_ATTN_ERR_INVALID, "set_launch_shape: l2_group_kib must be in [0, 2^40] and max_ctas >= 0 "
+                "(got %lld, %d)", l2_group_kib, max_ctas);
+  g_shape.l2_group_kib = l2_group_kib;
+  g_shape.max_ctas = max_ctas;
+  g_last_error.clear();
+  return PHANTOM_ATTN_OK;
+}
+
+int phantom_attn_get_launch_shape(long long* l2_group_kib, int* max_ctas) {
+  if (!l2_group_kib || !max_ctas) return fail(PHANTOM_ATTN_ERR_INVALID, "get_launch_shape: null output pointer");
+  *l2_group_kib = g_shape.l2_group_kib;
+  *max_ctas = g_shape.max_ctas;
   return PHANTOM_ATTN_OK;
 }
 

@@ -41,4 +41,12 @@ void note_launch();
 void timing_begin(cudaStream_t s);
 void timing_end(cudaStream_t s);
 
+// Launch-shape override of the tensor-core kernel for the calling thread (0 = automatic): K/V bytes per
+// L2 head group in KiB, and a cap on the persistent grid.
+struct LaunchShape {
+  long long l2_group_kib = 0;
+  int max_ctas = 0;
+};
+const LaunchShape& launch_shape();
+
 }  // namespace phantom

@@ -34,6 +34,8 @@ SIGNATURES = {
     "phantom_attn_launch_count": (ctypes.c_longlong, [_I]),
     "phantom_attn_kernel_timing": (_I, [_I]),
     "phantom_attn_kernel_timing_read": (_I, [ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_longlong)]),
+    "phantom_attn_set_launch_shape": (_I, [ctypes.c_longlong, _I]),
+    "phantom_attn_get_launch_shape": (_I, [ctypes.POINTER(ctypes.c_longlong), ctypes.POINTER(_I)]),
 }
 
 
@@ -136,3 +138,13 @@ class CAPI:
         ms, n = ctypes.c_double(0.0), ctypes.c_longlong(0)
         self._check(self.lib.phantom_attn_kernel_timing_read(ctypes.byref(ms), ctypes.byref(n)))
         return ms.value, n.value
+
+    def set_launch_shape(self, l2_group_kib: int = 0, max_ctas: int = 0) -> None:
+        """Launch-shape override of the tensor-core kernel on the calling thread (0 = automatic)."""
+        self._check(self.lib.phantom_attn_set_launch_shape(int(l2_group_kib), int(max_ctas)))
+
+    def get_launch_shape(self) -> tuple[int, int]:
+        """(l2_group_kib, max_ctas) of the calling thread; 0 = automatic."""
+        kib, ctas = ctypes.c_longlong(0), ctypes.c_int(0)
+        self._check(self.lib.phantom_attn_get_launch_shape(ctypes.byref(kib), ctypes.byref(ctas)))
+        return kib.value, ctas.value

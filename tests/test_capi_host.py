@@ -62,6 +62,30 @@ def test_launch_count_resets(lib):
     assert lib.launch_count() == 0
 
 
+def test_launch_shape_is_per_thread_and_validated(lib):
+    """The launch-shape override (host state only, no GPU) reads back, is per calling thread, and
+    rejects negative values and oversized groups with PHANTOM_ATTN_ERR_INVALID."""
+    import threading
+
+    from cuda_attn.capi import ERR_INVALID, CapiError
+    try:
+        assert lib.get_launch_shape() == (0, 0)
+        lib.set_launch_shape(4096, 17)
+        assert lib.get_launch_shape() == (4096, 17)
+        seen = []
+        t = threading.Thread(target=lambda: seen.append(lib.get_launch_shape()))
+        t.start()
+        t.join()
+        assert seen == [(0, 0)]
+        for kib, ctas in [(-1, 0), (0, -1), ((1 << 40) + 1, 0)]:
+            with pytest.raises(CapiError) as e:
+                lib.set_launch_shape(kib, ctas)
+            assert e.value.code == ERR_INVALID and "set_launch_shape" in str(e.value)
+        assert lib.get_launch_shape() == (4096, 17)
+    finally:
+        lib.set_launch_shape(0, 0)
+
+
 def test_python_api_mirrors_reference_names():
     import cuda_attn
     for name in ("naive", "tiled", "fused", "fused_tuned", "fused_vec", "fused_db", "fused_tc", "reference",

@@ -137,6 +137,27 @@ def test_bf16_fallback_heads_among_fp16_p_heads(capi):
         assert rel < 5e-3, (h, rel)
 
 
+@pytest.mark.parametrize("d", [64, 128])
+@pytest.mark.parametrize("causal", [False, True])
+def test_launch_shapes_give_identical_results(capi, d, causal):
+    """Every launch shape computes each unit the same way, so the output is bit-identical to the default
+    shape's: one CTA running all 96 units from the work counter, 7 CTAs, one head per L2 group, and all
+    heads in one group (bf16, so the staged-V path runs too). The default result matches the oracle."""
+    q, k, v = make_qkv(2, 24, 1000, d, torch.bfloat16, seed=31 + d)
+    try:
+        capi.set_launch_shape(0, 0)
+        base = run_capi(capi, "fused_tc", q, k, v, causal)
+        for kib, ctas in [(0, 1), (0, 7), (1, 0), (1 << 30, 0), (1, 5)]:
+            capi.set_launch_shape(kib, ctas)
+            assert capi.get_launch_shape() == (kib, ctas)
+            o = run_capi(capi, "fused_tc", q, k, v, causal)
+            assert torch.equal(o, base), (kib, ctas)
+    finally:
+        capi.set_launch_shape(0, 0)
+    ref = attention_naive(np64(q), np64(k), np64(v), causal)
+    assert_parity(np64(base), ref, "bfloat16", f"default launch shape d={d} causal={causal}")
+
+
 def test_non_default_stream(capi):
     q, k, v = make_qkv(1, 4, 777, 128, torch.bfloat16, seed=3)
     s = torch.cuda.Stream()
