@@ -188,7 +188,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
             const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmVh,
             const int* __restrict__ vflags, uint16_t* __restrict__ O, int BH, int N, float scale_log2, int causal,
-            int group_heads, int* __restrict__ status, int* __restrict__ work_ctr) {
+            int group_heads, int split_from, int* __restrict__ status, int* __restrict__ work_ctr) {
   using C = Cfg<D>;
   constexpr int BN = C::BN;
   extern __shared__ uint8_t smem_raw[];
@@ -219,21 +219,25 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
   // units and publishes each id in a shared-memory ring before arriving on q_full; the other roles
   // read it after their wait on q_full (they are at most one unit behind, so neither the phase nor the
   // ring slot can be overtaken). An id of -1 ends every role's loop.
+  // Query blocks from split_from on (host-chosen, all two-tile) are split into two one-tile units each,
+  // so that a last partial wave of r <= #CTAs/2 blocks becomes 2r short units, one per CTA.
   const int n_qtiles = (N + BM - 1) / BM;
   const int n_qblk = (n_qtiles + 1) / 2;
-  const int n_units = n_qblk * BH;
+  const int n_units = n_qblk * BH + (n_qblk * BH - split_from);
   struct Unit {
     int bh, row0, n_kv;
     bool has_b;
   };
   auto unit_of = [&](int u) {
     Unit x;
-    const int grp = u / (group_heads * n_qblk);
+    const bool split = u >= split_from;
+    const int blk = split ? split_from + ((u - split_from) >> 1) : u;
+    const int grp = blk / (group_heads * n_qblk);
     const int g_heads = min(group_heads, BH - grp * group_heads);
-    const int r_in = u - grp * group_heads * n_qblk;
+    const int r_in = blk - grp * group_heads * n_qblk;
     x.bh = grp * group_heads + r_in % g_heads;
-    const int qt0 = 2 * (n_qblk - 1 - r_in / g_heads);
-    x.has_b = qt0 + 1 < n_qtiles;
+    const int qt0 = 2 * (n_qblk - 1 - r_in / g_heads) + (split ? (u - split_from) & 1 : 0);
+    x.has_b = !split && qt0 + 1 < n_qtiles;
     x.row0 = qt0 * BM;
     const int kv_end = causal ? min(N, x.row0 + (x.has_b ? 2 * BM : BM)) : N;
     x.n_kv = (kv_end + BN - 1) / BN;
@@ -699,17 +703,33 @@ cudaError_t launch_t(const LaunchArgs& a, const CUtensorMap& mq, const CUtensorM
   const long long kv_bytes = 4LL * a.N * D;
   const long long group_bytes = shape.l2_group_kib > 0 ? shape.l2_group_kib << 10 : 16LL << 20;
   const int group_heads = (int)std::max(1LL, std::min((long long)a.BH, group_bytes / kv_bytes));
+  // Tail split (non-causal): a last partial wave of r query blocks with 2r <= CTAs runs as 2r one-tile
+  // units, one per CTA, instead of r two-tile units on r CTAs while the others idle. Only two-tile
+  // blocks are split: with an odd tile count the one-tile blocks are the first of each head group.
+  const long long n_blk = (long long)n_qblk * a.BH;
+  int split_from = (int)n_blk;
+  if (!a.causal && n_blk > grid.x) {
+    const long long r = n_blk % grid.x;
+    const long long n_groups = (a.BH + group_heads - 1) / group_heads;
+    const long long last_group = (n_groups - 1) * group_heads * n_qblk;
+    const long long last_heads = a.BH - (n_groups - 1) * group_heads;
+    const bool odd_tiles = n_qtiles % 2 != 0;
+    if (r > 0 && 2 * r <= grid.x && (!odd_tiles || n_blk - r >= last_group + last_heads) &&
+        2 * n_blk - (n_blk - r) <= 0x7fffffffLL)
+      split_from = (int)(n_blk - r);
+  }
   const float scale_log2 = 1.4426950408889634f / sqrtf((float)D);
   // Work counter of the persistent CTAs: the int 128 bytes into the (256-byte) status allocation. A
   // launch of one wave (units <= CTAs) never reads it, so only larger launches reset it.
   int* work_ctr = a.status + 32;
-  if ((long long)n_qblk * a.BH > (long long)grid.x) {
+  if (2 * n_blk - split_from > (long long)grid.x) {
     cudaError_t e0 = cudaMemsetAsync(work_ctr, 0, sizeof(int), a.stream);
     if (e0 != cudaSuccess) return e0;
   }
   timing_begin(a.stream);
   kern<<<grid, tc::NUM_THREADS, smem, a.stream>>>(mq, mk, mv, mvh, vflags, static_cast<uint16_t*>(a.o), a.BH, a.N,
-                                                   scale_log2, a.causal ? 1 : 0, group_heads, a.status, work_ctr);
+                                                   scale_log2, a.causal ? 1 : 0, group_heads, split_from, a.status,
+                                                   work_ctr);
   timing_end(a.stream);
   note_launch();
   return cudaGetLastError();

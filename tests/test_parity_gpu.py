@@ -139,15 +139,19 @@ def test_bf16_fallback_heads_among_fp16_p_heads(capi):
 
 @pytest.mark.parametrize("d", [64, 128])
 @pytest.mark.parametrize("causal", [False, True])
-def test_launch_shapes_give_identical_results(capi, d, causal):
-    """Every launch shape computes each unit the same way, so the output is bit-identical to the default
-    shape's: one CTA running all 96 units from the work counter, 7 CTAs, one head per L2 group, and all
-    heads in one group (bf16, so the staged-V path runs too). The default result matches the oracle."""
-    q, k, v = make_qkv(2, 24, 1000, d, torch.bfloat16, seed=31 + d)
+@pytest.mark.parametrize("heads,n", [(24, 1000), (20, 300)])
+def test_launch_shapes_give_identical_results(capi, d, causal, heads, n):
+    """Every launch shape computes each Q tile the same way, so the output is bit-identical to the
+    default shape's: one CTA running every unit from the work counter, 7, 11 or 13 CTAs, one head per L2
+    group, and all heads in one group (bf16, so the staged-V path runs too). Non-causal shapes whose last
+    partial wave is at most half the grid split its query blocks into one-tile units: at N = 1000 on the
+    148 CTAs of a B200 and on 5, 7 or 11 CTAs; at N = 300 (an odd tile count) on 7, 11 or 13 CTAs with
+    all heads in one group. The others do not. The default result matches the oracle."""
+    q, k, v = make_qkv(2, heads, n, d, torch.bfloat16, seed=31 + d + n)
     try:
         capi.set_launch_shape(0, 0)
         base = run_capi(capi, "fused_tc", q, k, v, causal)
-        for kib, ctas in [(0, 1), (0, 7), (1, 0), (1 << 30, 0), (1, 5)]:
+        for kib, ctas in [(0, 1), (0, 7), (0, 11), (0, 13), (1, 0), (1 << 30, 0), (1, 5), (1, 11)]:
             capi.set_launch_shape(kib, ctas)
             assert capi.get_launch_shape() == (kib, ctas)
             o = run_capi(capi, "fused_tc", q, k, v, causal)
