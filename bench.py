@@ -21,7 +21,8 @@ Printed on rank 0, one JSON line:
             back (head chunks pipelined over three streams), all inside the timed region.
   roofline  the tensor-core attention kernel alone (CUDA-event brackets around each of its launches in
             the timed region): algorithmic FLOPs per launch / average launch time, against the measured
-            sustained bf16 peak; traffic = DRAM bytes per launch from the committed ncu summary.
+            sustained bf16 peak; traffic = DRAM bytes per launch from the committed ncu summary of
+            config 4 (null for the other workloads, which that summary does not cover).
   cpu_baseline  the oracle port of the reference's CPU path (fp32 SDPA math on CPU) on a bounded sample.
 """
 from __future__ import annotations
@@ -45,6 +46,7 @@ for _p in (os.path.join(ROOT, "phantom-a100_b200"), ROOT):
 METRIC = "attention fwd TFLOP/s per GPU & % of B200 tensor peak at 1/2/4/8 GPUs"
 PEAKS_FILE = os.path.join(ROOT, "MEASURED_PEAKS.json")
 TRAFFIC_FILE = os.path.join(ROOT, "profiles", "attn_fwd_tc_config4_traffic.txt")
+TRAFFIC_WORKLOAD = "config4"  # the workload that summary was captured on; other workloads report null
 FALLBACK_PEAKS = {"bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "hbm_gbs": 6650.0}
 
 
@@ -375,7 +377,7 @@ def main():
         "pct_of_peak": {"sustained": 100.0 * value / world / peak_sus, "burst": 100.0 * value / world / peak_burst,
                         "peaks": peak_kind},
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak_sus, "unit": "TFLOP/s",
-                     "frac": (achieved / peak_sus) if achieved else None, "traffic": load_traffic(),
+                     "frac": (achieved / peak_sus) if achieved else None, "traffic": load_traffic() if base.name == TRAFFIC_WORKLOAD else None,
                      "kernel": "phantom::tc::attn_fwd_tc", "kernel_ms_avg": avg_kernel_ms,
                      "kernel_ms_avg_max_rank": kernel_ms_max, "flops_per_launch": flops_per_launch,
                      "peak_kind": f"{peak_kind} bf16 sustained (MEASURED_PEAKS.json bf16_tflops_sustained)",
