@@ -632,7 +632,7 @@ EncodeTiledFn encode_fn() {
 
 // (d, N, BH) view of a contiguous (BH, N, d) 16-bit array; 64 x rows x 1 boxes, 128-byte swizzle.
 // Rows past N read as zeros, per head.
-bool make_map(CUtensorMap* m, const void* base, int BH, int N, int d, bool bf16, int rows) {
+bool encode_map(CUtensorMap* m, const void* base, int BH, int N, int d, bool bf16, int rows) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return false;
   const cuuint64_t dims[3] = {(cuuint64_t)d, (cuuint64_t)N, (cuuint64_t)BH};
@@ -643,6 +643,36 @@ bool make_map(CUtensorMap* m, const void* base, int BH, int N, int d, bool bf16,
                   const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
+}
+
+// Per-thread cache of encoded maps. A map is a pure function of (base, BH, N, d, dtype, rows), so a
+// cached copy stays correct even after the caller frees and reuses an address; the cache only saves
+// the host-side encoding on calls that repeat their buffers.
+constexpr int kMapCache = 16;
+struct MapEntry {
+  CUtensorMap map;
+  const void* base = nullptr;
+  int BH = 0, N = 0, d = 0, rows = 0;
+  bool bf16 = false, valid = false;
+};
+thread_local MapEntry g_maps[kMapCache];
+thread_local int g_map_next = 0;
+
+bool make_map(CUtensorMap* m, const void* base, int BH, int N, int d, bool bf16, int rows) {
+  for (const MapEntry& e : g_maps)
+    if (e.valid && e.base == base && e.BH == BH && e.N == N && e.d == d && e.rows == rows && e.bf16 == bf16) {
+      *m = e.map;
+      return true;
+    }
+  if (!encode_map(m, base, BH, N, d, bf16, rows)) return false;
+  MapEntry& e = g_maps[g_map_next];
+  g_map_next = (g_map_next + 1) % kMapCache;
+  e.map = *m;
+  e.base = base;
+  e.BH = BH, e.N = N, e.d = d, e.rows = rows;
+  e.bf16 = bf16;
+  e.valid = true;
+  return true;
 }
 
 // Stream-ordered scratch for the bf16 V staging: one memory pool per device, owned by the library,
