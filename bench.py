@@ -384,7 +384,7 @@ def main():
                      "frac_of_burst": (achieved / peak_burst) if achieved else None},
         "e2e": {"value": total_flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms, "steps": e2e_steps,
-                "path": "pinned host -> cuda_attn.fused_tc_host (public API; copies overlapped with the kernel over 8 head chunks) -> pinned host", "matches_value_run": e2e_ok},
+                "path": "pinned host -> cuda_attn.fused_tc_host (public API; copies overlapped with the kernel over head chunks: 8 full, the last cut in halves) -> pinned host", "matches_value_run": e2e_ok},
         "gpu_launches": launches,
         "kernel_launches_timed": kernel_launches,
         "clocks": clocks,

@@ -2,10 +2,14 @@
 
     o = cuda_attn.fused_tc_host(q, k, v)      # q, k, v: (B, H, N, d) pinned CPU tensors -> O on the host
 
-Heads are independent, so the B*H heads are cut into chunks and streamed through two device slots on three
-CUDA streams: while chunk i is attended on the compute stream, chunk i+1 is copied host->device and chunk
-i-1 device->host. The host link (~50 GB/s per direction) rather than the kernel then bounds the call, and
-the two directions overlap each other. Each chunk runs the same C-ABI entry point as fused_tc.
+Heads are independent, so the B*H heads are cut into chunks and streamed through three device slots on
+three CUDA streams: while chunk i is attended on the compute stream, chunk i+1 is copied host->device and
+chunk i-1 device->host. The host link (~50 GB/s per direction) rather than the kernel then bounds the call,
+and the two directions overlap each other. Three slots let the copy of chunk i+2 start while chunk i's
+output is still in flight (the output copy shares the link with the input copies). The last full chunk is
+cut into halves (... per, per/2, per/4, ..., 1, 1 heads), so that the work left after the last input copy,
+the last chunk's attention and output copy, is small. Each chunk runs the same C-ABI entry point as
+fused_tc.
 """
 from __future__ import annotations
 
@@ -35,6 +39,27 @@ def _streams(device: torch.device):
     return s[key]
 
 
+def chunk_plan(bh: int, chunks: int) -> list[int]:
+    """Head counts of the chunks: full chunks of ceil(bh / chunks) heads, then the last one cut into
+    halves (4 -> 2, 1, 1), so the tail after the last input copy is one small chunk. chunks <= 1: one
+    chunk of all heads (no pipelining)."""
+    if chunks <= 1:
+        return [bh]
+    per = max(1, math.ceil(bh / chunks))
+    sizes = []
+    left = bh
+    while left > per:
+        sizes.append(per)
+        left -= per
+    while left > 1:
+        half = left // 2
+        sizes.append(left - half)
+        left = half
+    if left:
+        sizes.append(left)
+    return sizes
+
+
 def fused_tc_host(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool = False,
                   out: torch.Tensor | None = None, chunks: int = 8, device: int | torch.device | None = None,
                   synchronize: bool = True) -> torch.Tensor:
@@ -59,23 +84,24 @@ def fused_tc_host(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: boo
     if out is None:
         out = torch.empty(q.shape, dtype=q.dtype, pin_memory=True)
     hq, hk, hv, ho = (x.view(BH, N, d) for x in (q, k, v, out))
-    per = max(1, math.ceil(BH / max(1, chunks)))
-    n_chunks = math.ceil(BH / per)
+    sizes = chunk_plan(BH, chunks)
+    per = sizes[0]
+    n_slots = min(3, len(sizes))
     lib = _lib()
     with torch.cuda.device(dev):
         h2d, comp, d2h = _streams(dev)
         cur = torch.cuda.current_stream(dev)
-        slots = [[torch.empty((per, N, d), dtype=q.dtype, device=dev) for _ in range(4)] for _ in range(2)]
-        loaded = [torch.cuda.Event() for _ in range(2)]
-        computed = [torch.cuda.Event() for _ in range(2)]
-        freed = [torch.cuda.Event() for _ in range(2)]
+        slots = [[torch.empty((per, N, d), dtype=q.dtype, device=dev) for _ in range(4)] for _ in range(n_slots)]
+        loaded = [torch.cuda.Event() for _ in range(n_slots)]
+        computed = [torch.cuda.Event() for _ in range(n_slots)]
+        freed = [torch.cuda.Event() for _ in range(n_slots)]
         h2d.wait_stream(cur)  # inputs written by earlier work on the caller's stream are visible
-        for i in range(n_chunks):
-            s = i % 2
-            a, b = i * per, min(BH, (i + 1) * per)
-            n = b - a
+        b = 0
+        for i, n in enumerate(sizes):
+            s = i % n_slots
+            a, b = b, b + n
             dq, dk, dv, do = (x[:n] for x in slots[s])
-            if i >= 2:
+            if i >= n_slots:
                 h2d.wait_event(freed[s])
             with torch.cuda.stream(h2d):
                 dq.copy_(hq[a:b], non_blocking=True)
@@ -91,7 +117,7 @@ def fused_tc_host(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: boo
                 ho[a:b].copy_(do, non_blocking=True)
                 freed[s].record(d2h)
         cur.wait_stream(d2h)
-        for t in (slots[0] + slots[1]):
+        for t in (x for slot in slots for x in slot):
             t.record_stream(h2d)
             t.record_stream(comp)
             t.record_stream(d2h)

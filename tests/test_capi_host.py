@@ -111,3 +111,21 @@ def test_torch_binding_signatures():
     for arg in ("causal: bool = False", "double_buffer: bool = True", "br: ", "= 64", "bc: ", "= 32"):
         assert arg in doc
     assert "causal: bool = False" in ext.fused_tc.__doc__
+
+
+@pytest.mark.parametrize("bh,chunks", [(32, 8), (128, 8), (10, 3), (10, 1), (1, 8), (7, 8), (5, 3), (2, 8), (1000, 7)])
+def test_host_pipeline_chunk_plan(bh, chunks):
+    """fused_tc_host's chunk plan covers every head once: full chunks, then the last one cut into halves
+    down to one head (a short tail after the last input copy); one chunk when chunks <= 1."""
+    from cuda_attn.pipeline import chunk_plan
+    sizes = chunk_plan(bh, chunks)
+    assert sum(sizes) == bh and min(sizes) >= 1
+    if chunks <= 1:
+        assert sizes == [bh]
+        return
+    per = sizes[0]
+    assert per == -(-bh // chunks)
+    assert all(s <= per for s in sizes)
+    assert sizes == sorted(sizes, reverse=True)
+    if bh > 1:
+        assert sizes[-1] == 1
