@@ -77,7 +77,8 @@ int phantom_attn_fused_tc(const void* q, const void* k, const void* v, void* o, 
  * array's device address and zeroes the status word, synchronously), so make it before any stream
  * capture. Every call on a device shares the array: calls that overlap on the GPU (different streams,
  * or another thread) race on it and must be serialised by the caller. Bounded-wait expiries of this
- * path are recorded in its own status word, which phantom_attn_device_status() does not read.
+ * path are recorded in a status word inside the array; phantom_attn_device_status() reads and clears
+ * it (without allocating) and reports its bits together with PHANTOM_ATTN_STATUS_NOALLOC.
  */
 int phantom_attn_fused_tc_noalloc(const void* q, const void* k, const void* v, void* o, int BH, int N,
                                   int head_dim, int dtype, int causal, void* stream);
@@ -113,18 +114,23 @@ int phantom_attn_tiled(const void* q, const void* k, const void* v, void* o, int
                        int head_dim, int dtype, int causal, void* stream);
 
 /*
- * Reads and clears the device status word of the current device (synchronises the device).
+ * Reads and clears the device status words of the current device (synchronises the device).
  * *status = 0 when every kernel since the last call finished normally; otherwise a bit set of
- * where a bounded wait expired. No counterpart in the reference (its kernels had no waits).
+ * where a bounded wait expired: bits 0-3 (copy, MMA, softmax and epilogue waits of the tensor-core
+ * kernel), PHANTOM_ATTN_STATUS_PROBE (the test probe below), and PHANTOM_ATTN_STATUS_NOALLOC when
+ * the bits came from phantom_attn_fused_tc_noalloc's own word. Allocates nothing. No counterpart in
+ * the reference (its kernels had no waits).
  */
+#define PHANTOM_ATTN_STATUS_NOALLOC 256
 int phantom_attn_device_status(int* status);
 
 /*
  * Test support for the failure path: launches (asynchronously, on `stream`) a one-warp kernel that
  * waits, with the same bounded mbarrier wait the attention kernels use, on a barrier that nothing
  * arrives on. The wait gives up after its limit (about a second), and the kernel sets bit 16
- * (PHANTOM_ATTN_STATUS_PROBE) of the device status word and exits; the context stays usable, and
- * phantom_attn_device_status then reports and clears the bit. No counterpart in the reference.
+ * (PHANTOM_ATTN_STATUS_PROBE) of the device status word, and of phantom_attn_fused_tc_noalloc's word
+ * once that entry point has been called on the device, and exits; the context stays usable, and
+ * phantom_attn_device_status then reports and clears the bits. No counterpart in the reference.
  */
 #define PHANTOM_ATTN_STATUS_PROBE 16
 int phantom_attn_wait_expiry_probe(void* stream);

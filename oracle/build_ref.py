@@ -1,7 +1,8 @@
 """Build recipe for oracle/_ref/ - the reference's own harness, compiled from its sources in place.
 TEST INFRASTRUCTURE ONLY (a checker / comparison baseline, never the product).
 
-    python oracle/build_ref.py [--reference /path/to/Phantom-A100]
+    python oracle/build_ref.py --reference /path/to/Phantom-A100
+    PHANTOM_REFERENCE=/path/to/Phantom-A100 python oracle/build_ref.py
 
 Compiles b4batunde/Phantom-A100's sim/harness.cu (its torch-free driver: seeded fp16 inputs, every
 kernel v1..v4 from csrc/kernels/*.cuh, a float64 CPU check and a CUDA-event TIME line; harness.cu:1-167)
@@ -11,7 +12,7 @@ reference's recompiled WMMA kernel (fused_tc) be timed on a B200 beside the tcge
 
     HARNESS_ITERS=100 oracle/_ref/harness fused_tc 128 1024      # BASELINE config 2 (B*H=128, N=1024)
 
-Without a reference checkout this is a no-op.
+Without a reference checkout (no --reference, no PHANTOM_REFERENCE) this is a no-op.
 """
 from __future__ import annotations
 
@@ -24,7 +25,15 @@ OUT = os.path.join(HERE, "_ref")
 CUDA_HOME = os.environ.get("CUDA_HOME", "/usr/local/cuda")
 
 
-def build(reference: str = "/root/reference", force: bool = False) -> str | None:
+def reference_dir(reference: str | None = None) -> str | None:
+    """The reference checkout: the argument, else $PHANTOM_REFERENCE, else None."""
+    return reference or os.environ.get("PHANTOM_REFERENCE") or None
+
+
+def build(reference: str | None = None, force: bool = False) -> str | None:
+    reference = reference_dir(reference)
+    if reference is None:
+        return None
     src = os.path.join(reference, "sim", "harness.cu")
     if not os.path.exists(src):
         return None
@@ -42,7 +51,7 @@ def build(reference: str = "/root/reference", force: bool = False) -> str | None
 
 if __name__ == "__main__":
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=None, help="reference checkout (default: $PHANTOM_REFERENCE)")
     ap.add_argument("--force", action="store_true")
     a = ap.parse_args()
     print(build(a.reference, a.force) or "reference checkout not found; nothing built")

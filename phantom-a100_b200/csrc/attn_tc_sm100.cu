@@ -42,6 +42,7 @@
 #include <math_constants.h>
 
 #include <algorithm>
+#include <atomic>
 #include <mutex>
 
 #include "launchers.h"
@@ -130,11 +131,15 @@ __device__ __forceinline__ float row_max(const float (&s)[N]) {
 
 // V staging for bf16 inputs: Vh = fp16(V), per (head, chunk) flag = 1 if a finite V value of the
 // chunk lies outside the fp16 range (it would become inf). Grid (kVChunks, BH), 16-byte vectors.
+// It runs on the attention kernel's stream just before it, so it also zeroes that launch's work
+// counter (`ctr`, null when the launch does not use one).
 constexpr int kVChunks = 32;
 
 __global__ void __launch_bounds__(256)
-stage_v_f16(const uint4* __restrict__ V, uint4* __restrict__ Vh, int* __restrict__ flags, long long vec_per_head) {
+stage_v_f16(const uint4* __restrict__ V, uint4* __restrict__ Vh, int* __restrict__ flags, long long vec_per_head,
+            int* __restrict__ ctr) {
   const int bh = blockIdx.y;
+  if (ctr != nullptr && bh == 0 && blockIdx.x == 0 && threadIdx.x == 0) *ctr = 0;
   const long long per_chunk = (vec_per_head + kVChunks - 1) / kVChunks;
   const long long b = (long long)blockIdx.x * per_chunk;
   const long long e = min(vec_per_head, b + per_chunk);
@@ -161,6 +166,10 @@ stage_v_f16(const uint4* __restrict__ V, uint4* __restrict__ Vh, int* __restrict
 // polynomial exp2 on the FMA pipe, the others the MUFU ex2 unit (16 results per clock per SM). Measured
 // on configs 2-4 against 0, 1, 3 and 4 of every 8 pairs (and other placements of 2): 2 of 8 at {0, 3}
 // was fastest (+1.5% to +3.5% over 3 of 8).
+// The polynomial clamps its argument at -125, so a masked score (-inf) or one more than 125 below the
+// reference max gives 2^-125 instead of 0. In fp16 that rounds to 0, and in the row sum (>= 1) it is
+// absorbed, so only bf16 P (heads whose V exceeds the fp16 range, where |V| may reach 1e38) needs the
+// exact zero, which it gets here.
 template <bool P_BF16, int OFF, int N>
 __device__ __forceinline__ float softmax64(const float (&s)[N], float scale_log2, float m_sub, uint32_t (&p)[32]) {
   const float2 sc = make_float2(scale_log2, scale_log2), nm = make_float2(-m_sub, -m_sub);
@@ -169,7 +178,12 @@ __device__ __forceinline__ float softmax64(const float (&s)[N], float scale_log2
   for (int c = 0; c < 32; ++c) {
     float2 x = fma2(make_float2(s[OFF + 2 * c], s[OFF + 2 * c + 1]), sc, nm);
     if ((0x09 >> (c & 7)) & 1) {
+      const float2 arg = x;
       x = exp2_fma2(x);
+      if constexpr (P_BF16) {
+        x.x = arg.x < -125.f ? 0.f : x.x;
+        x.y = arg.y < -125.f ? 0.f : x.y;
+      }
     } else {
       x.x = ex2(x.x);
       x.y = ex2(x.y);
@@ -539,12 +553,17 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
           ++oc;
           tc_fence_after();
           if (__any_sync(0xffffffffu, need)) {
+            const float2 a2 = make_float2(alpha, alpha);  // 1 in rows that keep their reference max
 #pragma unroll
             for (int c = 0; c < D / 32; ++c) {
               uint32_t rr[32];
               tmem_ld32_wait(t_o + c * 32, rr);
 #pragma unroll
-              for (int i = 0; i < 32; ++i) rr[i] = __float_as_uint(__uint_as_float(rr[i]) * alpha);
+              for (int i = 0; i < 16; ++i) {
+                const float2 x = mul2(make_float2(__uint_as_float(rr[2 * i]), __uint_as_float(rr[2 * i + 1])), a2);
+                rr[2 * i] = __float_as_uint(x.x);
+                rr[2 * i + 1] = __float_as_uint(x.y);
+              }
               tmem_st32(t_o + c * 32, rr);
             }
           }
@@ -602,10 +621,12 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
 // Failure-path probe: one warp waits, with the same bounded mbarrier wait the attention kernel uses,
 // on a barrier that nothing arrives on. The wait gives up after kWaitLimitCycles, raises the abort
 // flag and ORs kErrProbeWait into the status word; a second wait then returns at once on the flag.
-// Nothing is left in flight (no copies, no MMAs, no TMEM), so the context stays usable.
+// `status2` (may be null): a second status word that gets the same bit once the wait has expired (the
+// allocation-free entry point's own word). Nothing is left in flight (no copies, no MMAs, no TMEM), so
+// the context stays usable.
 constexpr int kErrProbeWait = 16;
 
-__global__ void __launch_bounds__(32, 1) wait_expiry_probe(int* __restrict__ status) {
+__global__ void __launch_bounds__(32, 1) wait_expiry_probe(int* __restrict__ status, int* __restrict__ status2) {
   __shared__ uint64_t bar;
   __shared__ int abort_flag;
   if (threadIdx.x == 0) {
@@ -617,6 +638,7 @@ __global__ void __launch_bounds__(32, 1) wait_expiry_probe(int* __restrict__ sta
   const bool first = mbar_wait(smem_u32(&bar), 0, &abort_flag, status, kErrProbeWait);
   const bool second = mbar_wait(smem_u32(&bar), 0, &abort_flag, status, kErrProbeWait);
   if (threadIdx.x == 0 && (first || second)) atomicOr(status, 1 << 30);  // a wait completed: impossible
+  if (threadIdx.x == 0 && !first && status2 != nullptr) atomicOr(status2, kErrProbeWait);
 }
 
 }  // namespace tc
@@ -686,10 +708,10 @@ bool make_map(CUtensorMap* m, const void* base, int BH, int N, int d, bool bf16,
   return true;
 }
 
-// Stream-ordered scratch for the bf16 V staging: one memory pool per device, owned by the library,
-// that keeps freed blocks cached (release threshold = max) so repeated calls do not go back to the
-// driver. Allocation and free are ordered on the caller's stream, so concurrent calls on different
-// streams each get their own block.
+// Stream-ordered scratch of each launch (its work counter and, for bf16 inputs, the staged V): one
+// memory pool per device, owned by the library, that keeps freed blocks cached (release threshold =
+// max) so repeated calls do not go back to the driver. Allocation and free are ordered on the caller's
+// stream, so concurrent calls on different streams each get their own block.
 constexpr int kMaxDevices = 64;
 cudaMemPool_t g_pool[kMaxDevices] = {};
 std::mutex g_pool_mu;
@@ -714,114 +736,178 @@ cudaError_t device_pool(int dev, cudaMemPool_t* out) {
   return cudaSuccess;
 }
 
-template <int D, bool BF16>
-cudaError_t launch_t(const LaunchArgs& a, const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
-                     const CUtensorMap& mvh, const int* vflags) {
-  auto kern = tc::attn_fwd_tc<D, BF16>;
-  constexpr int smem = tc::Cfg<D>::SMEM_BYTES;
-  static bool attr_set[kMaxDevices] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < kMaxDevices && !attr_set[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if (e != cudaSuccess) return e;
-    attr_set[dev] = true;
-  }
+// Launch shape of one call: persistent grid, L2 head groups, tail split, and whether the CTAs take
+// units from a work counter (more units than CTAs).
+struct Plan {
+  unsigned grid = 0;
+  int group_heads = 1;
+  int split_from = 0;
+  bool uses_counter = false;
+};
+
+// Per-device launch facts, written once per device (std::atomic: several host threads may launch).
+std::atomic<bool> g_attr_set[2][kMaxDevices];
+std::atomic<int> g_sm_count[kMaxDevices];
+
+template <int D>
+cudaError_t make_plan(const LaunchArgs& a, int dev, Plan* p) {
   const int n_qtiles = (a.N + tc::BM - 1) / tc::BM;
   const int n_qblk = (n_qtiles + 1) / 2;
   if ((long long)n_qblk * a.BH > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
   // Persistent grid: one CTA per SM (at most one per work unit).
-  static int sm_count[kMaxDevices] = {};
-  if (dev < kMaxDevices && sm_count[dev] == 0) {
-    cudaError_t e = cudaDeviceGetAttribute(&sm_count[dev], cudaDevAttrMultiProcessorCount, dev);
+  int n_sm = g_sm_count[dev].load(std::memory_order_relaxed);
+  if (n_sm == 0) {
+    cudaError_t e = cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev);
     if (e != cudaSuccess) return e;
+    g_sm_count[dev].store(n_sm, std::memory_order_relaxed);
   }
   const LaunchShape& shape = launch_shape();
-  int n_sm = dev < kMaxDevices ? sm_count[dev] : 148;
   if (shape.max_ctas > 0) n_sm = std::min(n_sm, shape.max_ctas);
-  const dim3 grid((unsigned)std::min<long long>((long long)n_qblk * a.BH, n_sm));
+  const long long n_blk = (long long)n_qblk * a.BH;
+  p->grid = (unsigned)std::min<long long>(n_blk, n_sm);
   // Heads per scheduling group: K and V of a group (4*N*d bytes per head) within ~16 MiB of L2. The
   // persistent CTAs drift apart in their K/V streams, so a group's whole K/V is live in L2 at once; with
   // 48 MiB groups config 4 read its K/V 2-2.3x from DRAM, with 16 MiB once (ncu), at equal speed.
   const long long kv_bytes = 4LL * a.N * D;
   const long long group_bytes = shape.l2_group_kib > 0 ? shape.l2_group_kib << 10 : 16LL << 20;
-  const int group_heads = (int)std::max(1LL, std::min((long long)a.BH, group_bytes / kv_bytes));
+  p->group_heads = (int)std::max(1LL, std::min((long long)a.BH, group_bytes / kv_bytes));
   // Tail split (non-causal): a last partial wave of r query blocks with 2r <= CTAs runs as 2r one-tile
   // units, one per CTA, instead of r two-tile units on r CTAs while the others idle. Only two-tile
   // blocks are split: with an odd tile count the one-tile blocks are the first of each head group.
-  const long long n_blk = (long long)n_qblk * a.BH;
-  int split_from = (int)n_blk;
-  if (!a.causal && n_blk > grid.x) {
-    const long long r = n_blk % grid.x;
-    const long long n_groups = (a.BH + group_heads - 1) / group_heads;
-    const long long last_group = (n_groups - 1) * group_heads * n_qblk;
-    const long long last_heads = a.BH - (n_groups - 1) * group_heads;
+  p->split_from = (int)n_blk;
+  if (!a.causal && n_blk > p->grid) {
+    const long long r = n_blk % p->grid;
+    const long long n_groups = (a.BH + p->group_heads - 1) / p->group_heads;
+    const long long last_group = (n_groups - 1) * p->group_heads * n_qblk;
+    const long long last_heads = a.BH - (n_groups - 1) * p->group_heads;
     const bool odd_tiles = n_qtiles % 2 != 0;
-    if (r > 0 && 2 * r <= grid.x && (!odd_tiles || n_blk - r >= last_group + last_heads) &&
+    if (r > 0 && 2 * r <= p->grid && (!odd_tiles || n_blk - r >= last_group + last_heads) &&
         2 * n_blk - (n_blk - r) <= 0x7fffffffLL)
-      split_from = (int)(n_blk - r);
+      p->split_from = (int)(n_blk - r);
   }
+  // A launch of one wave (units <= CTAs) never reads the work counter.
+  p->uses_counter = 2 * n_blk - p->split_from > (long long)p->grid;
+  return cudaSuccess;
+}
+
+// Device memory one launch works in besides its inputs and output. `ctr`: the persistent CTAs' work
+// counter (only when the plan uses it; zeroed on the launch's stream before the kernel runs). `vh`,
+// `flags` (bf16 inputs only): the fp16 copy of V and its per-(head, chunk) fp16-overflow flags.
+struct Scratch {
+  int* ctr = nullptr;
+  void* vh = nullptr;
+  int* flags = nullptr;
+};
+
+template <int D, bool BF16>
+cudaError_t launch_t(const LaunchArgs& a, const Plan& p, const CUtensorMap& mq, const CUtensorMap& mk,
+                     const CUtensorMap& mv, const CUtensorMap& mvh, const Scratch& s, int dev) {
+  auto kern = tc::attn_fwd_tc<D, BF16>;
+  constexpr int smem = tc::Cfg<D>::SMEM_BYTES;
+  std::atomic<bool>& attr = g_attr_set[D == 128 ? 1 : 0][dev];
+  if (!attr.load(std::memory_order_acquire)) {
+    // Both BF16 instantiations of one head dimension share the shared-memory size; setting it twice is
+    // harmless, so two threads racing here need no lock.
+    cudaError_t e = cudaFuncSetAttribute(tc::attn_fwd_tc<D, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(tc::attn_fwd_tc<D, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    attr.store(true, std::memory_order_release);
+  }
+  if (p.uses_counter && s.ctr == nullptr) return cudaErrorInvalidValue;
   const float scale_log2 = 1.4426950408889634f / sqrtf((float)D);
-  // Work counter of the persistent CTAs: the int 128 bytes into the (256-byte) status allocation. A
-  // launch of one wave (units <= CTAs) never reads it, so only larger launches reset it.
-  int* work_ctr = a.status + 32;
-  if (2 * n_blk - split_from > (long long)grid.x) {
-    cudaError_t e0 = cudaMemsetAsync(work_ctr, 0, sizeof(int), a.stream);
-    if (e0 != cudaSuccess) return e0;
-  }
   timing_begin(a.stream);
-  kern<<<grid, tc::NUM_THREADS, smem, a.stream>>>(mq, mk, mv, mvh, vflags, static_cast<uint16_t*>(a.o), a.BH, a.N,
-                                                   scale_log2, a.causal ? 1 : 0, group_heads, split_from, a.status,
-                                                   work_ctr);
+  kern<<<p.grid, tc::NUM_THREADS, smem, a.stream>>>(mq, mk, mv, mvh, s.flags, static_cast<uint16_t*>(a.o), a.BH,
+                                                     a.N, scale_log2, a.causal ? 1 : 0, p.group_heads, p.split_from,
+                                                     a.status, s.ctr);
   timing_end(a.stream);
   note_launch();
   return cudaGetLastError();
 }
 
+// One call in the scratch `s`: zero the work counter (bf16: the V staging pass does it), stage V as fp16
+// (bf16), run the attention kernel.
 template <int D>
-cudaError_t launch_d(const LaunchArgs& a, const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv) {
-  if (a.dtype != PHANTOM_ATTN_BF16) return launch_t<D, false>(a, mq, mk, mv, mv, nullptr);
-  // bf16: stage V as fp16 in stream-ordered scratch [Vh | flags], run, release.
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return e;
-  cudaMemPool_t pool;
-  if ((e = device_pool(dev, &pool)) != cudaSuccess) return e;
-  const size_t vh_bytes = (size_t)a.BH * a.N * D * 2;
-  const size_t flag_bytes = (size_t)a.BH * tc::kVChunks * sizeof(int);
-  void* scratch = nullptr;
-  if ((e = cudaMallocFromPoolAsync(&scratch, vh_bytes + flag_bytes, pool, a.stream)) != cudaSuccess) return e;
-  void* vh = scratch;
-  int* flags = reinterpret_cast<int*>(static_cast<char*>(scratch) + vh_bytes);
+cudaError_t run_d(const LaunchArgs& a, const Plan& p, const CUtensorMap& mq, const CUtensorMap& mk,
+                  const CUtensorMap& mv, const Scratch& s, int dev) {
+  if (a.dtype != PHANTOM_ATTN_BF16) {
+    if (p.uses_counter) {
+      cudaError_t e = cudaMemsetAsync(s.ctr, 0, sizeof(int), a.stream);
+      if (e != cudaSuccess) return e;
+    }
+    return launch_t<D, false>(a, p, mq, mk, mv, mv, s, dev);
+  }
   const long long vec_per_head = (long long)a.N * D / 8;
   tc::stage_v_f16<<<dim3(tc::kVChunks, a.BH), 256, 0, a.stream>>>(
-      static_cast<const uint4*>(a.v), static_cast<uint4*>(vh), flags, vec_per_head);
+      static_cast<const uint4*>(a.v), static_cast<uint4*>(s.vh), s.flags, vec_per_head, s.ctr);
   note_launch();
-  e = cudaGetLastError();
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
   CUtensorMap mvh;
-  if (e == cudaSuccess && !make_map(&mvh, vh, a.BH, a.N, D, false, tc::Cfg<D>::BN)) e = cudaErrorInvalidValue;
-  if (e == cudaSuccess) e = launch_t<D, true>(a, mq, mk, mv, mvh, flags);
-  const cudaError_t ef = cudaFreeAsync(scratch, a.stream);
+  if (!make_map(&mvh, s.vh, a.BH, a.N, D, false, tc::Cfg<D>::BN)) return cudaErrorInvalidValue;
+  return launch_t<D, true>(a, p, mq, mk, mv, mvh, s, dev);
+}
+
+size_t staged_v_bytes(int BH, int N, int d) { return (size_t)BH * N * d * 2; }
+size_t flag_bytes(int BH) { return (size_t)BH * tc::kVChunks * sizeof(int); }
+constexpr size_t kCounterBytes = 256;  // keeps the staged V that follows 256-byte aligned
+
+// Allocating path: the launch's scratch [work counter | fp16 V | flags] is one block from the library's
+// stream-ordered pool, taken and released on the caller's stream. Launches that overlap on the GPU
+// (other streams, other threads) therefore never share a counter or a staging buffer.
+template <int D>
+cudaError_t launch_alloc(const LaunchArgs& a, const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
+                         int dev) {
+  Plan p;
+  cudaError_t e = make_plan<D>(a, dev, &p);
+  if (e != cudaSuccess) return e;
+  const bool bf16 = a.dtype == PHANTOM_ATTN_BF16;
+  const size_t ctr_bytes = p.uses_counter ? kCounterBytes : 0;
+  const size_t need = ctr_bytes + (bf16 ? staged_v_bytes(a.BH, a.N, D) + flag_bytes(a.BH) : 0);
+  if (need == 0) return run_d<D>(a, p, mq, mk, mv, Scratch{}, dev);
+  cudaMemPool_t pool;
+  if ((e = device_pool(dev, &pool)) != cudaSuccess) return e;
+  void* block = nullptr;
+  if ((e = cudaMallocFromPoolAsync(&block, need, pool, a.stream)) != cudaSuccess) return e;
+  char* base = static_cast<char*>(block);
+  Scratch s;
+  s.ctr = p.uses_counter ? reinterpret_cast<int*>(base) : nullptr;
+  if (bf16) {
+    s.vh = base + ctr_bytes;
+    s.flags = reinterpret_cast<int*>(base + ctr_bytes + staged_v_bytes(a.BH, a.N, D));
+  }
+  e = run_d<D>(a, p, mq, mk, mv, s, dev);
+  const cudaError_t ef = cudaFreeAsync(block, a.stream);
   return e != cudaSuccess ? e : ef;
 }
 
-// Same as launch_d, with the bf16 staging buffer [Vh | flags] supplied by the caller (no allocation).
+// Caller-supplied scratch (no allocation): the work counter at `ctr`, [fp16 V | flags] at `scratch`.
 template <int D>
-cudaError_t launch_d_scratch(const LaunchArgs& a, const CUtensorMap& mq, const CUtensorMap& mk,
-                             const CUtensorMap& mv, void* scratch) {
-  if (a.dtype != PHANTOM_ATTN_BF16) return launch_t<D, false>(a, mq, mk, mv, mv, nullptr);
-  const size_t vh_bytes = (size_t)a.BH * a.N * D * 2;
-  void* vh = scratch;
-  int* flags = reinterpret_cast<int*>(static_cast<char*>(scratch) + vh_bytes);
-  const long long vec_per_head = (long long)a.N * D / 8;
-  tc::stage_v_f16<<<dim3(tc::kVChunks, a.BH), 256, 0, a.stream>>>(
-      static_cast<const uint4*>(a.v), static_cast<uint4*>(vh), flags, vec_per_head);
-  note_launch();
-  cudaError_t e = cudaGetLastError();
-  CUtensorMap mvh;
-  if (e == cudaSuccess && !make_map(&mvh, vh, a.BH, a.N, D, false, tc::Cfg<D>::BN)) e = cudaErrorInvalidValue;
-  if (e == cudaSuccess) e = launch_t<D, true>(a, mq, mk, mv, mvh, flags);
-  return e;
+cudaError_t launch_given(const LaunchArgs& a, const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
+                         int dev, int* ctr, void* scratch) {
+  Plan p;
+  cudaError_t e = make_plan<D>(a, dev, &p);
+  if (e != cudaSuccess) return e;
+  Scratch s;
+  s.ctr = ctr;
+  if (a.dtype == PHANTOM_ATTN_BF16) {
+    s.vh = scratch;
+    s.flags = reinterpret_cast<int*>(static_cast<char*>(scratch) + staged_v_bytes(a.BH, a.N, D));
+  }
+  return run_d<D>(a, p, mq, mk, mv, s, dev);
+}
+
+bool input_maps(const LaunchArgs& a, CUtensorMap* mq, CUtensorMap* mk, CUtensorMap* mv) {
+  const bool bf16 = a.dtype == PHANTOM_ATTN_BF16;
+  const int bn = a.d == 64 ? tc::Cfg<64>::BN : tc::Cfg<128>::BN;
+  return make_map(mq, a.q, a.BH, a.N, a.d, bf16, tc::BM) && make_map(mk, a.k, a.BH, a.N, a.d, bf16, bn) &&
+         make_map(mv, a.v, a.BH, a.N, a.d, bf16, bn);
+}
+
+cudaError_t current_dev(int* dev) {
+  cudaError_t e = cudaGetDevice(dev);
+  if (e != cudaSuccess) return e;
+  return (*dev < 0 || *dev >= kMaxDevices) ? cudaErrorInvalidDevice : cudaSuccess;
 }
 
 }  // namespace
@@ -830,31 +916,30 @@ size_t fused_tc_smem_bytes(int d) { return d == 64 ? tc::Cfg<64>::SMEM_BYTES : t
 
 size_t fused_tc_scratch_bytes(int BH, int N, int d, int dtype) {
   if (dtype != PHANTOM_ATTN_BF16) return 0;
-  return (size_t)BH * N * d * 2 + (size_t)BH * tc::kVChunks * sizeof(int);
+  return staged_v_bytes(BH, N, d) + flag_bytes(BH);
 }
 
-cudaError_t launch_fused_tc_sm100_scratch(const LaunchArgs& a, void* scratch) {
-  const bool bf16 = a.dtype == PHANTOM_ATTN_BF16;
-  const int bn = a.d == 64 ? tc::Cfg<64>::BN : tc::Cfg<128>::BN;
+cudaError_t launch_fused_tc_sm100_scratch(const LaunchArgs& a, int* work_ctr, void* scratch) {
+  int dev = 0;
+  cudaError_t e = current_dev(&dev);
+  if (e != cudaSuccess) return e;
   CUtensorMap mq, mk, mv;
-  if (!make_map(&mq, a.q, a.BH, a.N, a.d, bf16, tc::BM) || !make_map(&mk, a.k, a.BH, a.N, a.d, bf16, bn) ||
-      !make_map(&mv, a.v, a.BH, a.N, a.d, bf16, bn))
-    return cudaErrorInvalidValue;
-  return a.d == 64 ? launch_d_scratch<64>(a, mq, mk, mv, scratch) : launch_d_scratch<128>(a, mq, mk, mv, scratch);
+  if (!input_maps(a, &mq, &mk, &mv)) return cudaErrorInvalidValue;
+  return a.d == 64 ? launch_given<64>(a, mq, mk, mv, dev, work_ctr, scratch)
+                   : launch_given<128>(a, mq, mk, mv, dev, work_ctr, scratch);
 }
 
 cudaError_t launch_fused_tc_sm100(const LaunchArgs& a) {
-  const bool bf16 = a.dtype == PHANTOM_ATTN_BF16;
-  const int bn = a.d == 64 ? tc::Cfg<64>::BN : tc::Cfg<128>::BN;
+  int dev = 0;
+  cudaError_t e = current_dev(&dev);
+  if (e != cudaSuccess) return e;
   CUtensorMap mq, mk, mv;
-  if (!make_map(&mq, a.q, a.BH, a.N, a.d, bf16, tc::BM) || !make_map(&mk, a.k, a.BH, a.N, a.d, bf16, bn) ||
-      !make_map(&mv, a.v, a.BH, a.N, a.d, bf16, bn))
-    return cudaErrorInvalidValue;
-  return a.d == 64 ? launch_d<64>(a, mq, mk, mv) : launch_d<128>(a, mq, mk, mv);
+  if (!input_maps(a, &mq, &mk, &mv)) return cudaErrorInvalidValue;
+  return a.d == 64 ? launch_alloc<64>(a, mq, mk, mv, dev) : launch_alloc<128>(a, mq, mk, mv, dev);
 }
 
-cudaError_t launch_wait_expiry_probe(int* status, cudaStream_t stream) {
-  tc::wait_expiry_probe<<<1, 32, 0, stream>>>(status);
+cudaError_t launch_wait_expiry_probe(int* status, int* status2, cudaStream_t stream) {
+  tc::wait_expiry_probe<<<1, 32, 0, stream>>>(status, status2);
   note_launch();
   return cudaGetLastError();
 }

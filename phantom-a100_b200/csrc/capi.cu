@@ -57,7 +57,7 @@ struct Device {
 };
 
 // Current device, its properties and its 256-byte status region (allocated once per device, zeroed):
-// the status word at byte 0, the tensor-core kernel's work counter at byte 128.
+// the status word at byte 0.
 int current_device(const char* name, Device* out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -165,7 +165,7 @@ int simt_entry(const char* name, const void* q, const void* k, const void* v, vo
 // Scratch of phantom_attn_fused_tc_noalloc, laid out as [status region (256 B: status word; the
 // persistent CTAs' work counter at byte 128) | fp16 copy of V | V overflow flags]. A file-scope device
 // array: every GPU that loads this library holds these 64 MiB until the process exits. All calls on a
-// device share it.
+// device share it, the work counter included (each call zeroes it on its stream before its kernel).
 constexpr size_t kNoAllocScratchBytes = size_t(64) << 20;
 constexpr size_t kNoAllocStatusBytes = 256;
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
@@ -198,6 +198,15 @@ int noalloc_setup(const char* name, int dev, unsigned char** scratch, int* cc, i
   *cc = g_noalloc_cc[dev];
   *optin = g_noalloc_optin[dev];
   return PHANTOM_ATTN_OK;
+}
+
+// Reads and clears one status word (the device is already synchronised). Returns the CUDA error.
+cudaError_t take_status_word(int* word, int* out) {
+  *out = 0;
+  if (word == nullptr) return cudaSuccess;
+  cudaError_t e = cudaMemcpy(out, word, sizeof(int), cudaMemcpyDeviceToHost);
+  if (e == cudaSuccess && *out != 0) e = cudaMemset(word, 0, sizeof(int));
+  return e;
 }
 
 }  // namespace
@@ -305,9 +314,10 @@ int phantom_attn_fused_tc_noalloc(const void* q, const void* k, const void* v, v
   if (fused_tc_smem_bytes(head_dim) > (size_t)optin)
     return fail(PHANTOM_ATTN_ERR_UNSUPPORTED, "%s: needs %zu bytes of shared memory, GPU allows %d", name,
                 fused_tc_smem_bytes(head_dim), optin);
-  LaunchArgs a{q, k, v, o, BH, N, head_dim, dtype, causal != 0, static_cast<cudaStream_t>(stream),
-               reinterpret_cast<int*>(scratch)};
-  if ((e = launch_fused_tc_sm100_scratch(a, scratch + kNoAllocStatusBytes)) != cudaSuccess) return cuda_fail(name, e);
+  int* status_word = reinterpret_cast<int*>(scratch);
+  LaunchArgs a{q, k, v, o, BH, N, head_dim, dtype, causal != 0, static_cast<cudaStream_t>(stream), status_word};
+  if ((e = launch_fused_tc_sm100_scratch(a, status_word + 32, scratch + kNoAllocStatusBytes)) != cudaSuccess)
+    return cuda_fail(name, e);
   g_last_error.clear();
   return PHANTOM_ATTN_OK;
 }
@@ -315,15 +325,27 @@ int phantom_attn_fused_tc_noalloc(const void* q, const void* k, const void* v, v
 int phantom_attn_device_status(int* status) {
   if (status == nullptr) return fail(PHANTOM_ATTN_ERR_INVALID, "device_status: null output pointer");
   *status = 0;
-  Device dev;
-  int rc = current_device("device_status", &dev);
-  if (rc != PHANTOM_ATTN_OK) return rc;
-  cudaError_t e = cudaDeviceSynchronize();
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_fail("device_status", e);
-  int v = 0;
-  if ((e = cudaMemcpy(&v, dev.status, sizeof(int), cudaMemcpyDeviceToHost)) != cudaSuccess)
+  if (dev < 0 || dev >= kMaxDevices) return fail(PHANTOM_ATTN_ERR_INVALID, "device_status: device %d out of range", dev);
+  // Neither word is created here: a word that does not exist yet has recorded nothing, and a caller of
+  // the allocation-free entry point can read its expiries without this call allocating.
+  int* main_word = nullptr;
+  int* noalloc_word = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(g_mu);
+    main_word = g_status[dev];
+  }
+  {
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    noalloc_word = reinterpret_cast<int*>(g_noalloc_ptr[dev]);
+  }
+  if ((e = cudaDeviceSynchronize()) != cudaSuccess) return cuda_fail("device_status", e);
+  int v_main = 0, v_noalloc = 0;
+  if ((e = take_status_word(main_word, &v_main)) != cudaSuccess || (e = take_status_word(noalloc_word, &v_noalloc)) != cudaSuccess)
     return cuda_fail("device_status", e);
-  if (v != 0 && (e = cudaMemset(dev.status, 0, sizeof(int))) != cudaSuccess) return cuda_fail("device_status", e);
+  const int v = v_main | (v_noalloc != 0 ? v_noalloc | PHANTOM_ATTN_STATUS_NOALLOC : 0);
   *status = v;
   g_last_error.clear();
   return v == 0 ? PHANTOM_ATTN_OK : fail(PHANTOM_ATTN_ERR_DEVICE, "device status 0x%x: a bounded wait expired", v);
@@ -333,7 +355,12 @@ int phantom_attn_wait_expiry_probe(void* stream) {
   Device dev;
   int rc = current_device("wait_expiry_probe", &dev);
   if (rc != PHANTOM_ATTN_OK) return rc;
-  const cudaError_t e = launch_wait_expiry_probe(dev.status, static_cast<cudaStream_t>(stream));
+  int* noalloc_word = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    noalloc_word = reinterpret_cast<int*>(g_noalloc_ptr[dev.id]);
+  }
+  const cudaError_t e = launch_wait_expiry_probe(dev.status, noalloc_word, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail("wait_expiry_probe", e);
   g_last_error.clear();
   return PHANTOM_ATTN_OK;

@@ -22,16 +22,17 @@ struct LaunchArgs {
 cudaError_t launch_fused_tc_sm100(const LaunchArgs& a);
 // Dynamic shared memory the tensor-core kernel needs for head dim d.
 size_t fused_tc_smem_bytes(int d);
-// Tensor-core kernel with caller-supplied scratch for the bf16 V staging (no allocation inside);
-// fused_tc_scratch_bytes() is the size it needs (0 for fp16 inputs).
-cudaError_t launch_fused_tc_sm100_scratch(const LaunchArgs& a, void* scratch);
+// Tensor-core kernel with caller-supplied scratch (no allocation inside): `work_ctr` is the persistent
+// CTAs' work counter (one int, zeroed by the launch on its stream; calls that overlap on the GPU must not
+// share it), `scratch` the bf16 V staging buffer of fused_tc_scratch_bytes() bytes (0 for fp16 inputs).
+cudaError_t launch_fused_tc_sm100_scratch(const LaunchArgs& a, int* work_ctr, void* scratch);
 size_t fused_tc_scratch_bytes(int BH, int N, int d, int dtype);
 
 // CUDA-core fp32-arithmetic kernel. Any d in [1, 256], dtype F32/F16/BF16.
 cudaError_t launch_fused_simt(const LaunchArgs& a);
 // One-warp kernel whose bounded mbarrier wait must expire (nothing arrives on the barrier); sets bit 16
-// of *status (attn_tc_sm100.cu).
-cudaError_t launch_wait_expiry_probe(int* status, cudaStream_t stream);
+// of *status, and of *status2 when that is not null (attn_tc_sm100.cu).
+cudaError_t launch_wait_expiry_probe(int* status, int* status2, cudaStream_t stream);
 size_t fused_simt_smem_bytes(int d);
 
 // Number of kernel launches the library has made on this thread (benchmark accounting).

@@ -173,6 +173,64 @@ def test_non_default_stream(capi):
     assert_parity(np64(o), ref, "bfloat16", "non-default stream")
 
 
+# (BH, N, d, dtype) of the concurrent launches: each has more work units (query blocks of two 128-row
+# tiles) than a B200 has SMs, so its persistent CTAs take units from a work counter while the others run.
+CONCURRENT = [(64, 4096, 128, torch.bfloat16), (48, 4096, 128, torch.float16), (96, 2048, 64, torch.float16),
+              (80, 2048, 64, torch.bfloat16)]
+
+
+def test_overlapping_launches_on_four_streams(capi):
+    """Multi-wave launches queued on four streams at once overlap on the GPU. Each launch has its own
+    work counter (and bf16 staging buffer), so every launch computes all of its query blocks: each output
+    equals the same call made alone, bit for bit, and matches the oracle on sampled rows."""
+    inputs = [make_qkv(1, bh, n, d, dt, seed=60 + i) for i, (bh, n, d, dt) in enumerate(CONCURRENT)]
+    serial = [run_capi(capi, "fused_tc", q, k, v) for q, k, v in inputs]
+    streams = [torch.cuda.Stream() for _ in CONCURRENT]
+    for rep in range(3):
+        outs = [torch.full_like(q, float("nan")) for q, _, _ in inputs]
+        torch.cuda.synchronize()
+        for s, (q, k, v), o in zip(streams, inputs, outs):
+            capi.fused_tc(q, k, v, o, stream=s)  # queued back to back: the four kernels overlap
+        torch.cuda.synchronize()
+        for i, (o, ref) in enumerate(zip(outs, serial)):
+            assert torch.equal(o, ref), f"launch {i} (round {rep}) differs from the serial call"
+    rng = np.random.default_rng(5)
+    for (q, k, v), o, (bh, n, d, dt) in zip(inputs, serial, CONCURRENT):
+        rows = np.unique(np.concatenate([[0, n - 1], rng.choice(n, 24, replace=False)]))
+        for h in (0, bh - 1):
+            ref = sampled_rows_naive(np64(q[0, h]), np64(k[0, h]), np64(v[0, h]), rows)
+            assert_parity(np64(o[0, h])[rows], ref, torch_dtype_name(dt), f"BH={bh} N={n} d={d} head {h}")
+
+
+def test_two_threads_through_the_host_pipeline(capi):
+    """Two host threads run fused_tc_host at once (each on its own three streams): its full chunks (4 heads
+    at N = 16384, 6 heads at N = 8192) are 256 and 192 work units, so both threads' kernels use work
+    counters concurrently. Each result equals the device-resident call bit for bit."""
+    import threading
+    import cuda_attn
+    jobs = [make_qkv(1, 12, 16384, 128, torch.bfloat16, scale=0.5, seed=70),
+            make_qkv(1, 16, 8192, 128, torch.float16, seed=71)]
+    expect = [run_capi(capi, "fused_tc", q, k, v).cpu() for q, k, v in jobs]
+    host = [[x.cpu().pin_memory() for x in job] for job in jobs]
+    results, errors = [None, None], []
+
+    def work(i):
+        try:
+            for _ in range(2):
+                results[i] = cuda_attn.fused_tc_host(*host[i], chunks=3)
+        except Exception as e:  # reported by the main thread
+            errors.append(e)
+
+    threads = [threading.Thread(target=work, args=(i,)) for i in range(2)]
+    for t in threads:
+        t.start()
+    for t in threads:
+        t.join()
+    assert not errors, errors
+    for i in range(2):
+        assert torch.equal(results[i], expect[i]), f"thread {i} differs from the device-resident call"
+
+
 def test_reruns_are_bit_identical(capi):
     q, k, v = make_qkv(2, 4, 1500, 128, torch.bfloat16, seed=8)
     a = run_capi(capi, "fused_tc", q, k, v, True)
