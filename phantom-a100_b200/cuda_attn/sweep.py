@@ -16,10 +16,10 @@ from __future__ import annotations
 import argparse
 import csv
 import os
-import statistics
 import sys
 from datetime import datetime, timezone
 
+import numpy as np
 import torch
 import torch.nn.functional as F
 from torch.nn.attention import SDPBackend, sdpa_kernel
@@ -28,42 +28,44 @@ from . import KERNELS, fused_tuned, reference
 from .hw_counters import load_peaks
 
 
-def sdpa_math(q, k, v, causal):
+def sdpa_math_backend(q, k, v, causal):
+    """torch SDPA restricted to the math backend (materialises the N x N scores; calibration only)."""
     with sdpa_kernel(SDPBackend.MATH):
         return F.scaled_dot_product_attention(q, k, v, is_causal=causal)
 
 
-def sdpa_default(q, k, v, causal):
+def sdpa_library(q, k, v, causal):
+    """torch SDPA with its default backend choice (a library kernel; calibration only)."""
     return F.scaled_dot_product_attention(q, k, v, is_causal=causal)
 
 
 IMPLS = dict(KERNELS, fused_tuned_128x64=lambda q, k, v, c: fused_tuned(q, k, v, c, True, 128, 64),
-             sdpa_math=sdpa_math, sdpa_default=sdpa_default)
+             sdpa_math=sdpa_math_backend, sdpa_default=sdpa_library)
 TENSOR_CORE = {"fused_vec", "fused_db", "fused_tc", "fused_tuned_128x64"}
-MATERIALIZES_S = {"sdpa_math"}
 
 
 def attention_flops(b, h, n, d, causal):
-    f = 4.0 * b * h * n * n * d
-    return f / 2 if causal else f
+    """Two N x N x d matmuls per (batch, head): 2 * 2 * N^2 * d FLOPs; causal keeps half of them."""
+    return (0.5 if causal else 1.0) * 4.0 * b * h * n * n * d
 
 
 def time_cuda(fn, warmup, iters, flush_buf):
+    """Per-run device time of fn() in ms as (median, p10, p90). Every run is bracketed by its own event
+    pair on the current stream, with the L2 cache overwritten (flush_buf, larger than L2) just before the
+    pair; the runs are queued back to back and read after one synchronize, so host launch gaps between
+    runs do not enter the figures."""
     for _ in range(warmup):
         fn()
-    torch.cuda.synchronize()
-    times = []
-    for _ in range(iters):
-        flush_buf.zero_()
-        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s.record()
+    stream = torch.cuda.current_stream()
+    marks = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(iters)]
+    for start, stop in marks:
+        flush_buf.fill_(1)
+        start.record(stream)
         fn()
-        e.record()
-        torch.cuda.synchronize()
-        times.append(s.elapsed_time(e))
-    times.sort()
-    qs = statistics.quantiles(times, n=10) if len(times) >= 2 else [times[0]] * 9
-    return statistics.median(times), qs[0], qs[-1]
+        stop.record(stream)
+    stop.synchronize()
+    ms = np.array([a.elapsed_time(b) for a, b in marks])
+    return float(np.median(ms)), float(np.percentile(ms, 10)), float(np.percentile(ms, 90))
 
 
 def check(out, ref, dtype):
