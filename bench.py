@@ -436,7 +436,12 @@ def main():
     e2e_ms = max_over_ranks(f0.elapsed_time(f1)) / e2e_steps
     h2d = sum(x.numel() * x.element_size() for x in (hq, hk, hv))
     d2h = ho.numel() * ho.element_size()
-    e2e_ok = torch.equal(ho.to(dev), o)
+    # the host pipeline runs every query block over its whole K/V range; the device-resident run may have
+    # cut its last wave into K/V parts (few-wave launches), which agrees within tolerance, not bit for bit
+    ho_dev = ho.to(dev)
+    e2e_same = {"bitwise": bool(torch.equal(ho_dev, o))}
+    if not e2e_same["bitwise"]:
+        e2e_same["rel_l2"] = ((ho_dev.double() - o.double()).norm() / o.double().norm()).item()
 
     peaks, peak_kind = load_peaks()
     peak_sus = float(peaks.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"]))
@@ -489,7 +494,7 @@ def main():
                      "kernel_mcycles_at_median_sm_clock": avg_kernel_ms * sm_mhz * 1e-3 if avg_kernel_ms and sm_mhz else None},
         "e2e": {"value": total_flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms, "steps": e2e_steps,
-                "path": "pinned host -> cuda_attn.fused_tc_host (public API; copies overlapped with the kernel over head chunks: 8 full, the last cut in halves) -> pinned host", "matches_value_run": e2e_ok},
+                "path": "pinned host -> cuda_attn.fused_tc_host (public API; copies overlapped with the kernel over head chunks: 8 full, the last cut in halves) -> pinned host", "matches_value_run": e2e_same},
         "gpu_launches": launches,
         "kernel_launches_timed": kernel_launches,
         "clocks": clocks,

@@ -167,6 +167,20 @@ int phantom_attn_kernel_timing_read(double* total_ms, long long* launches);
 int phantom_attn_set_launch_shape(long long l2_group_kib, int max_ctas);
 int phantom_attn_get_launch_shape(long long* l2_group_kib, int* max_ctas);
 
+/*
+ * Tail balancing of the tensor-core kernel (fused_tc, fused_tuned) for the calling thread. No
+ * counterpart in the reference. The persistent CTAs run the query blocks in waves; when the last wave
+ * would leave more than half of the CTAs idle at its end and is too large for one-tile units, its blocks
+ * (non-causal only) are cut into 2-8 parts of their K/V range: each part leaves an unnormalised partial
+ * result in the launch's scratch, and the last part of each row to finish merges them (results within the
+ * usual tolerance of the whole-range computation, not bit-identical to it). allow = 1 (default) lets the
+ * library choose this; allow = 0 keeps every block whole, so the results of a call are bit-identical for
+ * every launch shape and GPU count. phantom_attn_fused_tc_noalloc never cuts K/V ranges.
+ * Returns PHANTOM_ATTN_ERR_INVALID for a value other than 0 or 1; the getter returns the current value.
+ */
+int phantom_attn_set_kv_parts(int allow);
+int phantom_attn_get_kv_parts(void);
+
 #ifdef __cplusplus
 }
 #endif

@@ -131,15 +131,11 @@ __device__ __forceinline__ float row_max(const float (&s)[N]) {
 
 // V staging for bf16 inputs: Vh = fp16(V), per (head, chunk) flag = 1 if a finite V value of the
 // chunk lies outside the fp16 range (it would become inf). Grid (kVChunks, BH), 16-byte vectors.
-// It runs on the attention kernel's stream just before it, so it also zeroes that launch's work
-// counter (`ctr`, null when the launch does not use one).
 constexpr int kVChunks = 32;
 
 __global__ void __launch_bounds__(256)
-stage_v_f16(const uint4* __restrict__ V, uint4* __restrict__ Vh, int* __restrict__ flags, long long vec_per_head,
-            int* __restrict__ ctr) {
+stage_v_f16(const uint4* __restrict__ V, uint4* __restrict__ Vh, int* __restrict__ flags, long long vec_per_head) {
   const int bh = blockIdx.y;
-  if (ctr != nullptr && bh == 0 && blockIdx.x == 0 && threadIdx.x == 0) *ctr = 0;
   const long long per_chunk = (vec_per_head + kVChunks - 1) / kVChunks;
   const long long b = (long long)blockIdx.x * per_chunk;
   const long long e = min(vec_per_head, b + per_chunk);
@@ -199,12 +195,27 @@ __device__ __forceinline__ float softmax64(const float (&s)[N], float scale_log2
 // Persistent: each CTA processes a sequence of work units (two 128-row Q tiles of one head); the K/V
 // ring, the S sequence and every barrier phase run on across units, so the next unit's Q is loaded and
 // its first S computed while the softmax warps still finish and write out the current unit.
-template <int D, bool BF16>
+// Last partial wave of a launch (host-chosen, see make_plan): query blocks from `from` on run as `pieces`
+// units each - one-tile units (kv == 0: piece = Q tile of the block), or parts of the K/V range
+// (kv == 1: piece p covers K/V tiles [p*n/P, (p+1)*n/P) of both Q tiles; each part leaves an unnormalised
+// partial result, and the last part to finish a row merges them). No tail: from = #blocks, pieces = 1.
+struct Tail {
+  int from;
+  int pieces;
+  int kv;
+  float4* part_o;   // kv: per (tail block, Q tile, part) the partial O, [D/4][BM] float4 (lane-contiguous)
+  float2* part_ml;  // kv: per (tail block, Q tile, part) the rows' (reference max, sum)
+  int* part_cnt;    // kv: per (tail block, Q tile, row) the parts finished; zeroed before the launch
+};
+
+// KV_PARTS: the launch's tail is cut into K/V parts (Tail::kv = 1). A separate instantiation, so that every
+// other launch runs a kernel without the parts' bookkeeping (measured: carrying it cost 2-5% per tile).
+template <int D, bool BF16, bool KV_PARTS>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
 attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
             const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmVh,
             const int* __restrict__ vflags, uint16_t* __restrict__ O, int BH, int N, float scale_log2, int causal,
-            int group_heads, int split_from, int* __restrict__ status, int* __restrict__ work_ctr) {
+            int group_heads, const Tail tail, int* __restrict__ status, int* __restrict__ work_ctr) {
   using C = Cfg<D>;
   constexpr int BN = C::BN;
   extern __shared__ uint8_t smem_raw[];
@@ -235,28 +246,49 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
   // units and publishes each id in a shared-memory ring before arriving on q_full; the other roles
   // read it after their wait on q_full (they are at most one unit behind, so neither the phase nor the
   // ring slot can be overtaken). An id of -1 ends every role's loop.
-  // Query blocks from split_from on (host-chosen, all two-tile) are split into two one-tile units each,
-  // so that a last partial wave of r <= #CTAs/2 blocks becomes 2r short units, one per CTA.
+  // Query blocks from tail.from on (host-chosen, all two-tile) run as tail.pieces units each: one-tile
+  // units, so that a last partial wave of r <= #CTAs/2 blocks becomes 2r short units, one per CTA; or
+  // parts of the K/V range, so that a last wave of r > #CTAs/2 blocks spreads over all CTAs.
   const int n_qtiles = (N + BM - 1) / BM;
   const int n_qblk = (n_qtiles + 1) / 2;
-  const int n_units = n_qblk * BH + (n_qblk * BH - split_from);
+  const int n_units = tail.from + (n_qblk * BH - tail.from) * tail.pieces;
   struct Unit {
-    int bh, row0, n_kv;
+    int bh, row0, kv0, n_kv;
+    int part, tb;  // K/V part of a tail block (-1: the whole K/V range), tail block index
     bool has_b;
   };
   auto unit_of = [&](int u) {
     Unit x;
-    const bool split = u >= split_from;
-    const int blk = split ? split_from + ((u - split_from) >> 1) : u;
+    const bool in_tail = u >= tail.from;
+    int blk, piece;
+    if constexpr (KV_PARTS) {
+      blk = in_tail ? tail.from + (u - tail.from) / tail.pieces : u;
+      piece = in_tail ? (u - tail.from) % tail.pieces : 0;
+    } else {  // the tail, if any, is one-tile units: two per block
+      blk = in_tail ? tail.from + ((u - tail.from) >> 1) : u;
+      piece = in_tail ? (u - tail.from) & 1 : 0;
+    }
+    const bool one_tile = !KV_PARTS && in_tail;
     const int grp = blk / (group_heads * n_qblk);
     const int g_heads = min(group_heads, BH - grp * group_heads);
     const int r_in = blk - grp * group_heads * n_qblk;
     x.bh = grp * group_heads + r_in % g_heads;
-    const int qt0 = 2 * (n_qblk - 1 - r_in / g_heads) + (split ? (u - split_from) & 1 : 0);
-    x.has_b = !split && qt0 + 1 < n_qtiles;
+    const int qt0 = 2 * (n_qblk - 1 - r_in / g_heads) + (one_tile ? piece : 0);
+    x.has_b = !one_tile && qt0 + 1 < n_qtiles;
     x.row0 = qt0 * BM;
     const int kv_end = causal ? min(N, x.row0 + (x.has_b ? 2 * BM : BM)) : N;
-    x.n_kv = (kv_end + BN - 1) / BN;
+    const int n_kv = (kv_end + BN - 1) / BN;
+    if constexpr (KV_PARTS) {
+      x.part = in_tail ? piece : -1;
+      x.tb = blk - tail.from;
+      x.kv0 = in_tail ? piece * n_kv / tail.pieces : 0;
+      x.n_kv = in_tail ? (piece + 1) * n_kv / tail.pieces - x.kv0 : n_kv;
+    } else {
+      x.part = -1;
+      x.tb = 0;
+      x.kv0 = 0;
+      x.n_kv = n_kv;
+    }
     return x;
   };
   // P.V precision of a head (warp-wide: one flag per lane): fp16 unless a V value of the head
@@ -356,7 +388,8 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
           if (elect_one()) {
             mbar_arrive_expect_tx(kv_full(s), C::KV_TILE);
             for (int c = 0; c < C::KBLK; ++c)
-              tma_load_3d(sbase + C::OFF_KV + s * C::KV_TILE + c * C::KV_SUB, m, kv_full(s), c * 64, (jt >> 1) * BN, x.bh);
+              tma_load_3d(sbase + C::OFF_KV + s * C::KV_TILE + c * C::KV_SUB, m, kv_full(s), c * 64,
+                          (x.kv0 + (jt >> 1)) * BN, x.bh);
           }
           __syncwarp();
         }
@@ -529,7 +562,7 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
         ld_row<BN>(t_s, s);
         tc_fence_before();
         mbar_arrive(s_free(C::SHARED_S ? 0 : g));  // the next Q.K^T may overwrite S now
-        const int j0 = j * BN;
+        const int j0 = (x.kv0 + j) * BN;  // x.kv0 = 0 without K/V parts
         if (j0 + BN > N || (causal && j0 + BN - 1 > tile_row0)) {
           // columns c >= lim lie past N or (causal) after this row
           const int lim = min(N, causal ? row + 1 : N) - j0;
@@ -589,20 +622,109 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
       if (!ok) break;
       ++oc;
       tc_fence_after();
-      const float inv_l = 1.f / l;
       uint16_t* out = O + ((size_t)x.bh * N + row) * D;
+      if (!KV_PARTS || x.part < 0) {
+        const float inv_l = 1.f / l;
 #pragma unroll
-      for (int c = 0; c < D / 32; ++c) {
-        uint32_t rr[32];
-        tmem_ld32_wait(t_o + c * 32, rr);
-        uint32_t w[16];
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t rr[32];
+          tmem_ld32_wait(t_o + c * 32, rr);
+          uint32_t w[16];
 #pragma unroll
-        for (int i = 0; i < 16; ++i)
-          w[i] = pack2<BF16>(__uint_as_float(rr[2 * i]) * inv_l, __uint_as_float(rr[2 * i + 1]) * inv_l);
-        if (row < N) {
-          uint4* dst = reinterpret_cast<uint4*>(out + c * 32);
+          for (int i = 0; i < 16; ++i)
+            w[i] = pack2<BF16>(__uint_as_float(rr[2 * i]) * inv_l, __uint_as_float(rr[2 * i + 1]) * inv_l);
+          if (row < N) {
+            uint4* dst = reinterpret_cast<uint4*>(out + c * 32);
 #pragma unroll
-          for (int i = 0; i < 4; ++i) dst[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+            for (int i = 0; i < 4; ++i) dst[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+          }
+        }
+      } else if constexpr (KV_PARTS) {
+        // K/V part of a tail block: leave this row's unnormalised O, reference max and sum for the merge,
+        // then count the part as done. The thread that finishes a row's last part merges all parts of
+        // that row (it waits for nothing: every other part has published its row before counting it):
+        //   m = max_p m_p,  O = sum_p 2^(m_p - m) O_p / sum_p 2^(m_p - m) l_p.
+        const int P = tail.pieces;
+        const size_t slot0 = ((size_t)x.tb * 2 + g) * P;  // part 0 of this Q tile of the tail block
+        float4* po = tail.part_o + slot0 * (BM * D / 4) + r_local;  // [part][D/4][BM]
+        float2* pml = tail.part_ml + slot0 * BM + r_local;          // [part][BM]
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t rr[32];
+          tmem_ld32_wait(t_o + c * 32, rr);
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            __stcg(po + ((size_t)x.part * (D / 4) + c * 8 + i) * BM,
+                   make_float4(__uint_as_float(rr[4 * i]), __uint_as_float(rr[4 * i + 1]),
+                               __uint_as_float(rr[4 * i + 2]), __uint_as_float(rr[4 * i + 3])));
+        }
+        __stcg(pml + (size_t)x.part * BM, make_float2(m_used, l));
+        __threadfence();
+        const bool last = atomicAdd(tail.part_cnt + ((size_t)x.tb * 2 + g) * BM + r_local, 1) == P - 1;
+        if (__any_sync(0xffffffffu, last)) {  // the TMEM loads below are warp-collective
+          __threadfence();
+          // The merge runs over the parts in their fixed order 0..P-1, this thread's own part taken from
+          // TMEM (bit-identical to what it published), so the result does not depend on which part
+          // finished last.
+          constexpr int kMaxParts = 8;
+          float wq[kMaxParts];  // each part's reference max, then its weight 2^(m_q - m)
+          float m = m_used;
+#pragma unroll
+          for (int q = 0; q < kMaxParts; ++q) {
+            wq[q] = m_used;
+            if (q < P && q != x.part && last) wq[q] = __ldcg(pml + (size_t)q * BM).x;
+            if (q < P) m = fmaxf(m, wq[q]);
+          }
+          float lt = 0.f;
+#pragma unroll
+          for (int q = 0; q < kMaxParts; ++q) {
+            if (q < P) {
+              wq[q] = ex2(wq[q] - m);
+              const float lq = q == x.part ? l : (last ? __ldcg(pml + (size_t)q * BM).y : 0.f);
+              lt = fmaf(wq[q], lq, lt);
+            }
+          }
+          const float inv_l = 1.f / lt;
+#pragma unroll
+          for (int c = 0; c < D / 32; ++c) {
+            uint32_t rr[32];
+            tmem_ld32_wait(t_o + c * 32, rr);
+            if (last) {
+#pragma unroll
+              for (int h = 0; h < 2; ++h) {  // 16 columns at a time
+                float acc[16];
+#pragma unroll
+                for (int i = 0; i < 16; ++i) acc[i] = 0.f;
+#pragma unroll
+                for (int q = 0; q < kMaxParts; ++q) {
+                  if (q < P) {
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                      const int e = 16 * h + 4 * i;  // first column (within the chunk) of this float4
+                      float4 v;
+                      if (q == x.part)
+                        v = make_float4(__uint_as_float(rr[e]), __uint_as_float(rr[e + 1]), __uint_as_float(rr[e + 2]),
+                                        __uint_as_float(rr[e + 3]));
+                      else
+                        v = __ldcg(po + ((size_t)q * (D / 4) + c * 8 + 4 * h + i) * BM);
+                      acc[4 * i] = fmaf(wq[q], v.x, acc[4 * i]);
+                      acc[4 * i + 1] = fmaf(wq[q], v.y, acc[4 * i + 1]);
+                      acc[4 * i + 2] = fmaf(wq[q], v.z, acc[4 * i + 2]);
+                      acc[4 * i + 3] = fmaf(wq[q], v.w, acc[4 * i + 3]);
+                    }
+                  }
+                }
+                uint32_t w[8];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) w[i] = pack2<BF16>(acc[2 * i] * inv_l, acc[2 * i + 1] * inv_l);
+                if (row < N) {
+                  uint4* dst = reinterpret_cast<uint4*>(out + c * 32 + 16 * h);
+                  dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+                  dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+                }
+              }
+            }
+          }
         }
       }
       tc_fence_before();
@@ -736,21 +858,47 @@ cudaError_t device_pool(int dev, cudaMemPool_t* out) {
   return cudaSuccess;
 }
 
-// Launch shape of one call: persistent grid, L2 head groups, tail split, and whether the CTAs take
-// units from a work counter (more units than CTAs).
+// Launch shape of one call: persistent grid, L2 head groups, the last partial wave's split (tail), and
+// whether the CTAs take units from a work counter (more units than CTAs).
 struct Plan {
   unsigned grid = 0;
   int group_heads = 1;
-  int split_from = 0;
+  int tail_from = 0;    // first query block of the tail (= #blocks: no tail)
+  int tail_pieces = 1;  // units per tail block
+  bool tail_kv = false; // pieces are K/V parts (else one-tile units)
+  int n_tail = 0;       // tail blocks
   bool uses_counter = false;
 };
+
+// K/V parts per tail block: the fewest parts P (2..8, at least kMinPartTiles K/V tiles each) that minimise
+// the tail's length ceil(r*P/G)/P (in units of one block's time), used only if the launch's predicted length
+// falls by at least kMinPartGain: waves + 1 -> waves + that length. The parts cost time of their own (the
+// K/V-part instantiation runs ~2% slower per tile, and each part writes and the last one reads partial
+// results), and the units of earlier waves end at staggered times, so the last wave is less idle than this
+// count says: config 4 on one B200 (13 full waves + 124 of 148 blocks, predicted -1%) measured 2.6% slower
+// with 7 parts, while a launch of 1 full wave + 108 blocks (config 4 on 8 GPUs) is predicted 12.5% faster.
+constexpr int kMaxParts = 8;
+constexpr int kMinPartTiles = 4;
+constexpr double kMinPartGain = 0.08;
+int kv_parts(long long waves, long long r, long long grid, int n_kv) {
+  int best = 1;
+  double best_len = 1.0;
+  for (int P = 2; P <= kMaxParts && n_kv / P >= kMinPartTiles; ++P) {
+    const double len = (double)((r * P + grid - 1) / grid) / P;
+    if (len < best_len - 1e-9) {
+      best_len = len;
+      best = P;
+    }
+  }
+  return (waves + 1.0) / (waves + best_len) >= 1.0 + kMinPartGain ? best : 1;
+}
 
 // Per-device launch facts, written once per device (std::atomic: several host threads may launch).
 std::atomic<bool> g_attr_set[2][kMaxDevices];
 std::atomic<int> g_sm_count[kMaxDevices];
 
 template <int D>
-cudaError_t make_plan(const LaunchArgs& a, int dev, Plan* p) {
+cudaError_t make_plan(const LaunchArgs& a, int dev, bool allow_kv_parts, Plan* p) {
   const int n_qtiles = (a.N + tc::BM - 1) / tc::BM;
   const int n_qblk = (n_qtiles + 1) / 2;
   if ((long long)n_qblk * a.BH > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
@@ -771,75 +919,108 @@ cudaError_t make_plan(const LaunchArgs& a, int dev, Plan* p) {
   const long long kv_bytes = 4LL * a.N * D;
   const long long group_bytes = shape.l2_group_kib > 0 ? shape.l2_group_kib << 10 : 16LL << 20;
   p->group_heads = (int)std::max(1LL, std::min((long long)a.BH, group_bytes / kv_bytes));
-  // Tail split (non-causal): a last partial wave of r query blocks with 2r <= CTAs runs as 2r one-tile
-  // units, one per CTA, instead of r two-tile units on r CTAs while the others idle. Only two-tile
-  // blocks are split: with an odd tile count the one-tile blocks are the first of each head group.
-  p->split_from = (int)n_blk;
+  // Tail (non-causal): a last partial wave of r query blocks with 2r <= CTAs runs as 2r one-tile units,
+  // one per CTA, instead of r two-tile units on r CTAs while the others idle. Only two-tile blocks are
+  // split: with an odd tile count the one-tile blocks are the first of each head group. A larger last
+  // wave (r > CTAs/2, e.g. config 4 on 8 GPUs: 256 blocks on 148 CTAs) has its blocks' K/V ranges cut
+  // into P parts (kv_parts), so that its r*P shorter units spread over every CTA.
+  p->tail_from = (int)n_blk;
+  p->tail_pieces = 1;
+  p->tail_kv = false;
   if (!a.causal && n_blk > p->grid) {
     const long long r = n_blk % p->grid;
     const long long n_groups = (a.BH + p->group_heads - 1) / p->group_heads;
     const long long last_group = (n_groups - 1) * p->group_heads * n_qblk;
     const long long last_heads = a.BH - (n_groups - 1) * p->group_heads;
     const bool odd_tiles = n_qtiles % 2 != 0;
-    if (r > 0 && 2 * r <= p->grid && (!odd_tiles || n_blk - r >= last_group + last_heads) &&
-        2 * n_blk - (n_blk - r) <= 0x7fffffffLL)
-      p->split_from = (int)(n_blk - r);
+    const bool two_tile_tail = !odd_tiles || n_blk - r >= last_group + last_heads;
+    const int n_kv = (a.N + tc::Cfg<D>::BN - 1) / tc::Cfg<D>::BN;
+    if (r > 0 && 2 * r <= p->grid && two_tile_tail && n_blk + r <= 0x7fffffffLL) {
+      p->tail_from = (int)(n_blk - r);
+      p->tail_pieces = 2;
+    } else if (r > 0 && allow_kv_parts && launch_shape().kv_parts && two_tile_tail) {
+      const int P = kv_parts(n_blk / p->grid, r, p->grid, n_kv);
+      if (P > 1 && n_blk + r * (P - 1) <= 0x7fffffffLL) {
+        p->tail_from = (int)(n_blk - r);
+        p->tail_pieces = P;
+        p->tail_kv = true;
+      }
+    }
   }
+  p->n_tail = (int)n_blk - p->tail_from;
   // A launch of one wave (units <= CTAs) never reads the work counter.
-  p->uses_counter = 2 * n_blk - p->split_from > (long long)p->grid;
+  p->uses_counter = (long long)p->tail_from + (long long)p->n_tail * p->tail_pieces > (long long)p->grid;
   return cudaSuccess;
 }
 
 // Device memory one launch works in besides its inputs and output. `ctr`: the persistent CTAs' work
-// counter (only when the plan uses it; zeroed on the launch's stream before the kernel runs). `vh`,
-// `flags` (bf16 inputs only): the fp16 copy of V and its per-(head, chunk) fp16-overflow flags.
+// counter followed by the K/V-part counters (n_tail * 2 * 128 ints; both zeroed on the launch's stream
+// before the kernel runs). `part_o`, `part_ml`: the K/V parts' partial results. `vh`, `flags` (bf16 inputs
+// only): the fp16 copy of V and its per-(head, chunk) fp16-overflow flags.
 struct Scratch {
   int* ctr = nullptr;
+  float4* part_o = nullptr;
+  float2* part_ml = nullptr;
   void* vh = nullptr;
   int* flags = nullptr;
 };
 
+size_t round256(size_t b) { return (b + 255) & ~size_t(255); }
+// Bytes of the counters (zeroed before each launch) and of the K/V parts' partial results of a plan, 0 when
+// unused; counter_bytes() is the 256-byte-aligned room they take in an allocation.
+size_t counters_used(const Plan& p) {
+  if (!p.uses_counter && !p.tail_kv) return 0;
+  return sizeof(int) * (1 + (p.tail_kv ? (size_t)p.n_tail * 2 * tc::BM : 0));
+}
+size_t counter_bytes(const Plan& p) { return round256(counters_used(p)); }
+size_t part_o_bytes(const Plan& p, int d) {
+  return p.tail_kv ? (size_t)p.n_tail * 2 * p.tail_pieces * tc::BM * d * sizeof(float) : 0;
+}
+size_t part_ml_bytes(const Plan& p) {
+  return p.tail_kv ? round256((size_t)p.n_tail * 2 * p.tail_pieces * tc::BM * sizeof(float2)) : 0;
+}
+
 template <int D, bool BF16>
 cudaError_t launch_t(const LaunchArgs& a, const Plan& p, const CUtensorMap& mq, const CUtensorMap& mk,
                      const CUtensorMap& mv, const CUtensorMap& mvh, const Scratch& s, int dev) {
-  auto kern = tc::attn_fwd_tc<D, BF16>;
+  auto kern = p.tail_kv ? tc::attn_fwd_tc<D, BF16, true> : tc::attn_fwd_tc<D, BF16, false>;
   constexpr int smem = tc::Cfg<D>::SMEM_BYTES;
   std::atomic<bool>& attr = g_attr_set[D == 128 ? 1 : 0][dev];
   if (!attr.load(std::memory_order_acquire)) {
-    // Both BF16 instantiations of one head dimension share the shared-memory size; setting it twice is
+    // Every instantiation of one head dimension has the same shared-memory size; setting it twice is
     // harmless, so two threads racing here need no lock.
-    cudaError_t e = cudaFuncSetAttribute(tc::attn_fwd_tc<D, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(tc::attn_fwd_tc<D, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    cudaError_t e = cudaSuccess;
+    for (auto f : {tc::attn_fwd_tc<D, false, false>, tc::attn_fwd_tc<D, true, false>, tc::attn_fwd_tc<D, false, true>,
+                   tc::attn_fwd_tc<D, true, true>})
+      if (e == cudaSuccess) e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     attr.store(true, std::memory_order_release);
   }
-  if (p.uses_counter && s.ctr == nullptr) return cudaErrorInvalidValue;
+  if ((p.uses_counter && s.ctr == nullptr) || (p.tail_kv && (s.part_o == nullptr || s.part_ml == nullptr)))
+    return cudaErrorInvalidValue;
   const float scale_log2 = 1.4426950408889634f / sqrtf((float)D);
+  tc::Tail tail{p.tail_from, p.tail_pieces, p.tail_kv ? 1 : 0, s.part_o, s.part_ml, s.ctr ? s.ctr + 1 : nullptr};
   timing_begin(a.stream);
   kern<<<p.grid, tc::NUM_THREADS, smem, a.stream>>>(mq, mk, mv, mvh, s.flags, static_cast<uint16_t*>(a.o), a.BH,
-                                                     a.N, scale_log2, a.causal ? 1 : 0, p.group_heads, p.split_from,
+                                                     a.N, scale_log2, a.causal ? 1 : 0, p.group_heads, tail,
                                                      a.status, s.ctr);
   timing_end(a.stream);
   note_launch();
   return cudaGetLastError();
 }
 
-// One call in the scratch `s`: zero the work counter (bf16: the V staging pass does it), stage V as fp16
-// (bf16), run the attention kernel.
+// One call in the scratch `s`: zero the counters, stage V as fp16 (bf16), run the attention kernel.
 template <int D>
 cudaError_t run_d(const LaunchArgs& a, const Plan& p, const CUtensorMap& mq, const CUtensorMap& mk,
                   const CUtensorMap& mv, const Scratch& s, int dev) {
-  if (a.dtype != PHANTOM_ATTN_BF16) {
-    if (p.uses_counter) {
-      cudaError_t e = cudaMemsetAsync(s.ctr, 0, sizeof(int), a.stream);
-      if (e != cudaSuccess) return e;
-    }
-    return launch_t<D, false>(a, p, mq, mk, mv, mv, s, dev);
+  if (const size_t cb = counters_used(p)) {
+    cudaError_t e = cudaMemsetAsync(s.ctr, 0, cb, a.stream);
+    if (e != cudaSuccess) return e;
   }
+  if (a.dtype != PHANTOM_ATTN_BF16) return launch_t<D, false>(a, p, mq, mk, mv, mv, s, dev);
   const long long vec_per_head = (long long)a.N * D / 8;
   tc::stage_v_f16<<<dim3(tc::kVChunks, a.BH), 256, 0, a.stream>>>(
-      static_cast<const uint4*>(a.v), static_cast<uint4*>(s.vh), s.flags, vec_per_head, s.ctr);
+      static_cast<const uint4*>(a.v), static_cast<uint4*>(s.vh), s.flags, vec_per_head);
   note_launch();
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
@@ -850,20 +1031,19 @@ cudaError_t run_d(const LaunchArgs& a, const Plan& p, const CUtensorMap& mq, con
 
 size_t staged_v_bytes(int BH, int N, int d) { return (size_t)BH * N * d * 2; }
 size_t flag_bytes(int BH) { return (size_t)BH * tc::kVChunks * sizeof(int); }
-constexpr size_t kCounterBytes = 256;  // keeps the staged V that follows 256-byte aligned
 
-// Allocating path: the launch's scratch [work counter | fp16 V | flags] is one block from the library's
-// stream-ordered pool, taken and released on the caller's stream. Launches that overlap on the GPU
-// (other streams, other threads) therefore never share a counter or a staging buffer.
+// Allocating path: the launch's scratch [counters | K/V-part partials | fp16 V | flags] is one block from
+// the library's stream-ordered pool, taken and released on the caller's stream. Launches that overlap on
+// the GPU (other streams, other threads) therefore never share a counter or a buffer.
 template <int D>
 cudaError_t launch_alloc(const LaunchArgs& a, const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
                          int dev) {
   Plan p;
-  cudaError_t e = make_plan<D>(a, dev, &p);
+  cudaError_t e = make_plan<D>(a, dev, true, &p);
   if (e != cudaSuccess) return e;
   const bool bf16 = a.dtype == PHANTOM_ATTN_BF16;
-  const size_t ctr_bytes = p.uses_counter ? kCounterBytes : 0;
-  const size_t need = ctr_bytes + (bf16 ? staged_v_bytes(a.BH, a.N, D) + flag_bytes(a.BH) : 0);
+  const size_t cb = counter_bytes(p), ob = part_o_bytes(p, D), mb = part_ml_bytes(p);
+  const size_t need = cb + ob + mb + (bf16 ? staged_v_bytes(a.BH, a.N, D) + flag_bytes(a.BH) : 0);
   if (need == 0) return run_d<D>(a, p, mq, mk, mv, Scratch{}, dev);
   cudaMemPool_t pool;
   if ((e = device_pool(dev, &pool)) != cudaSuccess) return e;
@@ -871,22 +1051,27 @@ cudaError_t launch_alloc(const LaunchArgs& a, const CUtensorMap& mq, const CUten
   if ((e = cudaMallocFromPoolAsync(&block, need, pool, a.stream)) != cudaSuccess) return e;
   char* base = static_cast<char*>(block);
   Scratch s;
-  s.ctr = p.uses_counter ? reinterpret_cast<int*>(base) : nullptr;
+  if (cb) s.ctr = reinterpret_cast<int*>(base);
+  if (ob) {
+    s.part_o = reinterpret_cast<float4*>(base + cb);
+    s.part_ml = reinterpret_cast<float2*>(base + cb + ob);
+  }
   if (bf16) {
-    s.vh = base + ctr_bytes;
-    s.flags = reinterpret_cast<int*>(base + ctr_bytes + staged_v_bytes(a.BH, a.N, D));
+    s.vh = base + cb + ob + mb;
+    s.flags = reinterpret_cast<int*>(base + cb + ob + mb + staged_v_bytes(a.BH, a.N, D));
   }
   e = run_d<D>(a, p, mq, mk, mv, s, dev);
   const cudaError_t ef = cudaFreeAsync(block, a.stream);
   return e != cudaSuccess ? e : ef;
 }
 
-// Caller-supplied scratch (no allocation): the work counter at `ctr`, [fp16 V | flags] at `scratch`.
+// Caller-supplied scratch (no allocation): the work counter at `ctr`, [fp16 V | flags] at `scratch`. The
+// tail is never cut into K/V parts here (their partial results would need more scratch).
 template <int D>
 cudaError_t launch_given(const LaunchArgs& a, const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
                          int dev, int* ctr, void* scratch) {
   Plan p;
-  cudaError_t e = make_plan<D>(a, dev, &p);
+  cudaError_t e = make_plan<D>(a, dev, false, &p);
   if (e != cudaSuccess) return e;
   Scratch s;
   s.ctr = ctr;

@@ -405,6 +405,15 @@ int phantom_attn_get_launch_shape(long long* l2_group_kib, int* max_ctas) {
   return PHANTOM_ATTN_OK;
 }
 
+int phantom_attn_set_kv_parts(int allow) {
+  if (allow != 0 && allow != 1) return fail(PHANTOM_ATTN_ERR_INVALID, "set_kv_parts: allow must be 0 or 1 (got %d)", allow);
+  g_shape.kv_parts = allow;
+  g_last_error.clear();
+  return PHANTOM_ATTN_OK;
+}
+
+int phantom_attn_get_kv_parts(void) { return g_shape.kv_parts; }
+
 long long phantom_attn_launch_count(int reset) {
   const long long n = g_launches;
   if (reset) g_launches = 0;

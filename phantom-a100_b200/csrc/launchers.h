@@ -43,10 +43,13 @@ void timing_begin(cudaStream_t s);
 void timing_end(cudaStream_t s);
 
 // Launch-shape override of the tensor-core kernel for the calling thread (0 = automatic): K/V bytes per
-// L2 head group in KiB, and a cap on the persistent grid.
+// L2 head group in KiB, a cap on the persistent grid, and whether a last partial wave may be cut into
+// K/V parts (1, the default) or not (0: every query block then runs over its whole K/V range, so results
+// are bit-identical for every launch shape).
 struct LaunchShape {
   long long l2_group_kib = 0;
   int max_ctas = 0;
+  int kv_parts = 1;
 };
 const LaunchShape& launch_shape();
 

@@ -36,6 +36,8 @@ SIGNATURES = {
     "phantom_attn_kernel_timing_read": (_I, [ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_longlong)]),
     "phantom_attn_set_launch_shape": (_I, [ctypes.c_longlong, _I]),
     "phantom_attn_get_launch_shape": (_I, [ctypes.POINTER(ctypes.c_longlong), ctypes.POINTER(_I)]),
+    "phantom_attn_set_kv_parts": (_I, [_I]),
+    "phantom_attn_get_kv_parts": (_I, []),
 }
 
 
@@ -142,6 +144,14 @@ class CAPI:
     def set_launch_shape(self, l2_group_kib: int = 0, max_ctas: int = 0) -> None:
         """Launch-shape override of the tensor-core kernel on the calling thread (0 = automatic)."""
         self._check(self.lib.phantom_attn_set_launch_shape(int(l2_group_kib), int(max_ctas)))
+
+    def set_kv_parts(self, allow: bool) -> None:
+        """Whether a last partial wave may be cut into K/V parts (calling thread; default True). False keeps
+        results bit-identical for every launch shape and GPU count."""
+        self._check(self.lib.phantom_attn_set_kv_parts(int(bool(allow))))
+
+    def get_kv_parts(self) -> bool:
+        return bool(self.lib.phantom_attn_get_kv_parts())
 
     def get_launch_shape(self) -> tuple[int, int]:
         """(l2_group_kib, max_ctas) of the calling thread; 0 = automatic."""

@@ -9,7 +9,10 @@ and the two directions overlap each other. Three slots let the copy of chunk i+2
 output is still in flight (the output copy shares the link with the input copies). The last full chunk is
 cut into halves (... per, per/2, per/4, ..., 1, 1 heads), so that the work left after the last input copy,
 the last chunk's attention and output copy, is small. Each chunk runs the same C-ABI entry point as
-fused_tc.
+fused_tc, with the tail's K/V parts turned off (phantom_attn_set_kv_parts(0) on this thread for the
+duration of the call): the call is bound by the host link, not by the kernel's last wave, and every query
+block then runs over its whole K/V range, so the result equals a device-resident fused_tc call without
+K/V parts bit for bit, however the heads are chunked.
 """
 from __future__ import annotations
 
@@ -88,10 +91,19 @@ def fused_tc_host(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: boo
     per = sizes[0]
     n_slots = min(3, len(sizes))
     lib = _lib()
+    kv_parts = lib.get_kv_parts()
+    lib.set_kv_parts(False)
+    try:
+        return _pipeline(lib, hq, hk, hv, ho, out, sizes, per, n_slots, N, d, q.dtype, causal, dev, synchronize)
+    finally:
+        lib.set_kv_parts(kv_parts)
+
+
+def _pipeline(lib, hq, hk, hv, ho, out, sizes, per, n_slots, N, d, dtype, causal, dev, synchronize):
     with torch.cuda.device(dev):
         h2d, comp, d2h = _streams(dev)
         cur = torch.cuda.current_stream(dev)
-        slots = [[torch.empty((per, N, d), dtype=q.dtype, device=dev) for _ in range(4)] for _ in range(n_slots)]
+        slots = [[torch.empty((per, N, d), dtype=dtype, device=dev) for _ in range(4)] for _ in range(n_slots)]
         loaded = [torch.cuda.Event() for _ in range(n_slots)]
         computed = [torch.cuda.Event() for _ in range(n_slots)]
         freed = [torch.cuda.Event() for _ in range(n_slots)]

@@ -150,6 +150,7 @@ def test_launch_shapes_give_identical_results(capi, d, causal, heads, n):
     q, k, v = make_qkv(2, heads, n, d, torch.bfloat16, seed=31 + d + n)
     try:
         capi.set_launch_shape(0, 0)
+        capi.set_kv_parts(False)  # every block over its whole K/V range: identical for every shape
         base = run_capi(capi, "fused_tc", q, k, v, causal)
         for kib, ctas in [(0, 1), (0, 7), (0, 11), (0, 13), (1, 0), (1 << 30, 0), (1, 5), (1, 11)]:
             capi.set_launch_shape(kib, ctas)
@@ -158,8 +159,65 @@ def test_launch_shapes_give_identical_results(capi, d, causal, heads, n):
             assert torch.equal(o, base), (kib, ctas)
     finally:
         capi.set_launch_shape(0, 0)
+        capi.set_kv_parts(True)
     ref = attention_naive(np64(q), np64(k), np64(v), causal)
     assert_parity(np64(base), ref, "bfloat16", f"default launch shape d={d} causal={causal}")
+
+
+# (B*H, N, d, dtype, persistent-grid cap): launches of few waves whose last partial wave (more than half the
+# grid) the library cuts into K/V parts on a B200 (148 SMs): 256 blocks on 148 CTAs (4 parts), 384 blocks
+# (5 parts, d = 64), 192 blocks on a 120-CTA grid (5 parts) and 160 blocks on a 100-CTA grid (3 parts).
+KV_PART_CASES = [(32, 2048, 128, torch.bfloat16, 0), (24, 4096, 64, torch.float16, 0),
+                 (12, 4096, 128, torch.float16, 120), (20, 2048, 128, torch.bfloat16, 100)]
+
+
+@pytest.mark.parametrize("bh,n,d,dtype,cap", KV_PART_CASES)
+def test_tail_kv_parts_match_the_oracle(capi, bh, n, d, dtype, cap):
+    """The tail's query blocks run as K/V parts whose partial results the last-finishing part merges: the
+    output matches the oracle (every row of the first query blocks, where the tail lies, and sampled rows
+    elsewhere), differs from the whole-range computation only within tolerance, and is the same on a
+    rerun."""
+    q, k, v = make_qkv(1, bh, n, d, dtype, scale=0.5 if dtype == torch.bfloat16 else 1.0, seed=90 + n + d)
+    try:
+        capi.set_launch_shape(0, cap)
+        parts = run_capi(capi, "fused_tc", q, k, v)
+        again = run_capi(capi, "fused_tc", q, k, v)
+        capi.set_kv_parts(False)
+        whole = run_capi(capi, "fused_tc", q, k, v)
+    finally:
+        capi.set_launch_shape(0, 0)
+        capi.set_kv_parts(True)
+    assert torch.equal(parts, again), "rerun differs"
+    assert not torch.equal(parts, whole), "no K/V parts ran (plan did not cut the tail)"
+    rng = np.random.default_rng(bh + n)
+    rows = np.unique(np.concatenate([np.arange(0, 256), rng.choice(n, 48, replace=False)]))
+    for h in sorted({0, bh // 2, bh - 1}):
+        ref = sampled_rows_naive(np64(q[0, h]), np64(k[0, h]), np64(v[0, h]), rows)
+        assert_parity(np64(parts[0, h])[rows], ref, torch_dtype_name(dtype), f"K/V parts head {h}")
+        assert_parity(np64(whole[0, h])[rows], ref, torch_dtype_name(dtype), f"whole range head {h}")
+
+
+def test_tail_kv_parts_with_a_bf16_fallback_head(capi):
+    """A head whose V exceeds the fp16 range (bf16 P) inside a K/V-parted tail: its parts use bf16 P
+    throughout and merge to a finite result close to the truth."""
+    q, k, v = make_qkv(1, 32, 2048, 128, torch.bfloat16, scale=0.5, seed=95)
+    v[0, 31, 77, 5] = 2.0e6
+    o = run_capi(capi, "fused_tc", q, k, v)
+    assert torch.isfinite(o).all()
+    rows = np.arange(0, 256)
+    ref = sampled_rows_naive(np64(q[0, 31]), np64(k[0, 31]), np64(v[0, 31]), rows)
+    rel = np.linalg.norm(np64(o[0, 31])[rows] - ref) / np.linalg.norm(ref)
+    assert rel < 5e-3, rel
+    ref0 = sampled_rows_naive(np64(q[0, 0]), np64(k[0, 0]), np64(v[0, 0]), rows)
+    assert_parity(np64(o[0, 0])[rows], ref0, "bfloat16", "fp16-P head beside it")
+
+
+def test_kv_parts_switch_rejects_other_values(capi):
+    from cuda_attn.capi import ERR_INVALID
+    assert capi.get_kv_parts() is True
+    rc = capi.lib.phantom_attn_set_kv_parts(2)
+    assert rc == ERR_INVALID and "0 or 1" in capi.last_error()
+    assert capi.get_kv_parts() is True
 
 
 def test_non_default_stream(capi):
