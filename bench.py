@@ -210,10 +210,9 @@ def time_cpu_reference(cfg, heads, rows, threads):
 
 def cpu_baseline(cfg, seconds_target, threads):
     """The CPU baseline on a sample of about `seconds_target` seconds: whole heads (all query rows) from
-    head 0 on, as many as the rate measured on a first probe allows, at most all of the config's heads."""
-    probe_rows = min(cfg.N, 1024)
-    dt, fl = time_cpu_reference(cfg, 1, probe_rows, threads)
-    head_s = dt * cfg.N / probe_rows
+    head 0 on, as many as the rate of a first, untimed head (which also warms the thread pool) allows, at
+    most all of the config's heads."""
+    head_s, _ = time_cpu_reference(cfg, 1, cfg.N, threads)
     heads = int(max(1, min(cfg.BH, round(seconds_target / max(head_s, 1e-6)))))
     dt, fl = time_cpu_reference(cfg, heads, cfg.N, threads)
     return {"value": fl / dt / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": "port",

@@ -198,15 +198,24 @@ __device__ __forceinline__ float softmax64(const float (&s)[N], float scale_log2
 // Last partial wave of a launch (host-chosen, see make_plan): query blocks from `from` on run as `pieces`
 // units each - one-tile units (kv == 0: piece = Q tile of the block), or parts of the K/V range
 // (kv == 1: piece p covers K/V tiles [p*n/P, (p+1)*n/P) of both Q tiles; each part leaves an unnormalised
-// partial result, and the last part to finish a row merges them). No tail: from = #blocks, pieces = 1.
+// partial result, which merge_kv_parts combines after the launch). No tail: from = #blocks, pieces = 1.
 struct Tail {
   int from;
   int pieces;
   int kv;
   float4* part_o;   // kv: per (tail block, Q tile, part) the partial O, [D/4][BM] float4 (lane-contiguous)
   float2* part_ml;  // kv: per (tail block, Q tile, part) the rows' (reference max, sum)
-  int* part_cnt;    // kv: per (tail block, Q tile, row) the parts finished; zeroed before the launch
 };
+
+// (head, first query row) of query block `blk` in the unit order: heads in L2 groups of group_heads,
+// inside a group the blocks from the last query block to the first (all heads of a group interleaved).
+__device__ __forceinline__ void block_coords(int blk, int BH, int n_qblk, int group_heads, int* bh, int* qt0) {
+  const int grp = blk / (group_heads * n_qblk);
+  const int g_heads = min(group_heads, BH - grp * group_heads);
+  const int r_in = blk - grp * group_heads * n_qblk;
+  *bh = grp * group_heads + r_in % g_heads;
+  *qt0 = 2 * (n_qblk - 1 - r_in / g_heads);
+}
 
 // KV_PARTS: the launch's tail is cut into K/V parts (Tail::kv = 1). A separate instantiation, so that every
 // other launch runs a kernel without the parts' bookkeeping (measured: carrying it cost 2-5% per tile).
@@ -269,11 +278,9 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
       piece = in_tail ? (u - tail.from) & 1 : 0;
     }
     const bool one_tile = !KV_PARTS && in_tail;
-    const int grp = blk / (group_heads * n_qblk);
-    const int g_heads = min(group_heads, BH - grp * group_heads);
-    const int r_in = blk - grp * group_heads * n_qblk;
-    x.bh = grp * group_heads + r_in % g_heads;
-    const int qt0 = 2 * (n_qblk - 1 - r_in / g_heads) + (one_tile ? piece : 0);
+    int qt0;
+    block_coords(blk, BH, n_qblk, group_heads, &x.bh, &qt0);
+    qt0 += one_tile ? piece : 0;
     x.has_b = !one_tile && qt0 + 1 < n_qtiles;
     x.row0 = qt0 * BM;
     const int kv_end = causal ? min(N, x.row0 + (x.has_b ? 2 * BM : BM)) : N;
@@ -538,7 +545,7 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
     for (int nu = 0;; ++nu) {
       const int u = next_unit(nu, ok);
       if (u < 0) break;
-      const Unit x = unit_of(u);
+      Unit x = unit_of(u);
       if (g == 1 && !x.has_b) continue;
       const bool pv_bf16 = head_pv_bf16(x.bh);
       const int n_kv = x.n_kv;
@@ -622,6 +629,7 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
       if (!ok) break;
       ++oc;
       tc_fence_after();
+      if constexpr (KV_PARTS) x = unit_of(u);  // derived again: fewer registers live across the tile loop
       uint16_t* out = O + ((size_t)x.bh * N + row) * D;
       if (!KV_PARTS || x.part < 0) {
         const float inv_l = 1.f / l;
@@ -640,92 +648,19 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
           }
         }
       } else if constexpr (KV_PARTS) {
-        // K/V part of a tail block: leave this row's unnormalised O, reference max and sum for the merge,
-        // then count the part as done. The thread that finishes a row's last part merges all parts of
-        // that row (it waits for nothing: every other part has published its row before counting it):
-        //   m = max_p m_p,  O = sum_p 2^(m_p - m) O_p / sum_p 2^(m_p - m) l_p.
-        const int P = tail.pieces;
-        const size_t slot0 = ((size_t)x.tb * 2 + g) * P;  // part 0 of this Q tile of the tail block
-        float4* po = tail.part_o + slot0 * (BM * D / 4) + r_local;  // [part][D/4][BM]
-        float2* pml = tail.part_ml + slot0 * BM + r_local;          // [part][BM]
+        // K/V part of a tail block: leave this row's unnormalised O, reference max and sum; merge_kv_parts,
+        // launched after this kernel on the same stream, combines the parts and writes the row of O.
+        float4* po = tail.part_o + ((((size_t)x.tb * 2 + g) * tail.pieces + x.part) * (D / 4)) * BM + r_local;
 #pragma unroll
         for (int c = 0; c < D / 32; ++c) {
           uint32_t rr[32];
           tmem_ld32_wait(t_o + c * 32, rr);
 #pragma unroll
           for (int i = 0; i < 8; ++i)
-            __stcg(po + ((size_t)x.part * (D / 4) + c * 8 + i) * BM,
-                   make_float4(__uint_as_float(rr[4 * i]), __uint_as_float(rr[4 * i + 1]),
-                               __uint_as_float(rr[4 * i + 2]), __uint_as_float(rr[4 * i + 3])));
+            po[(size_t)(c * 8 + i) * BM] = make_float4(__uint_as_float(rr[4 * i]), __uint_as_float(rr[4 * i + 1]),
+                                                       __uint_as_float(rr[4 * i + 2]), __uint_as_float(rr[4 * i + 3]));
         }
-        __stcg(pml + (size_t)x.part * BM, make_float2(m_used, l));
-        __threadfence();
-        const bool last = atomicAdd(tail.part_cnt + ((size_t)x.tb * 2 + g) * BM + r_local, 1) == P - 1;
-        if (__any_sync(0xffffffffu, last)) {  // the TMEM loads below are warp-collective
-          __threadfence();
-          // The merge runs over the parts in their fixed order 0..P-1, this thread's own part taken from
-          // TMEM (bit-identical to what it published), so the result does not depend on which part
-          // finished last.
-          constexpr int kMaxParts = 8;
-          float wq[kMaxParts];  // each part's reference max, then its weight 2^(m_q - m)
-          float m = m_used;
-#pragma unroll
-          for (int q = 0; q < kMaxParts; ++q) {
-            wq[q] = m_used;
-            if (q < P && q != x.part && last) wq[q] = __ldcg(pml + (size_t)q * BM).x;
-            if (q < P) m = fmaxf(m, wq[q]);
-          }
-          float lt = 0.f;
-#pragma unroll
-          for (int q = 0; q < kMaxParts; ++q) {
-            if (q < P) {
-              wq[q] = ex2(wq[q] - m);
-              const float lq = q == x.part ? l : (last ? __ldcg(pml + (size_t)q * BM).y : 0.f);
-              lt = fmaf(wq[q], lq, lt);
-            }
-          }
-          const float inv_l = 1.f / lt;
-#pragma unroll
-          for (int c = 0; c < D / 32; ++c) {
-            uint32_t rr[32];
-            tmem_ld32_wait(t_o + c * 32, rr);
-            if (last) {
-#pragma unroll
-              for (int h = 0; h < 2; ++h) {  // 16 columns at a time
-                float acc[16];
-#pragma unroll
-                for (int i = 0; i < 16; ++i) acc[i] = 0.f;
-#pragma unroll
-                for (int q = 0; q < kMaxParts; ++q) {
-                  if (q < P) {
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                      const int e = 16 * h + 4 * i;  // first column (within the chunk) of this float4
-                      float4 v;
-                      if (q == x.part)
-                        v = make_float4(__uint_as_float(rr[e]), __uint_as_float(rr[e + 1]), __uint_as_float(rr[e + 2]),
-                                        __uint_as_float(rr[e + 3]));
-                      else
-                        v = __ldcg(po + ((size_t)q * (D / 4) + c * 8 + 4 * h + i) * BM);
-                      acc[4 * i] = fmaf(wq[q], v.x, acc[4 * i]);
-                      acc[4 * i + 1] = fmaf(wq[q], v.y, acc[4 * i + 1]);
-                      acc[4 * i + 2] = fmaf(wq[q], v.z, acc[4 * i + 2]);
-                      acc[4 * i + 3] = fmaf(wq[q], v.w, acc[4 * i + 3]);
-                    }
-                  }
-                }
-                uint32_t w[8];
-#pragma unroll
-                for (int i = 0; i < 8; ++i) w[i] = pack2<BF16>(acc[2 * i] * inv_l, acc[2 * i + 1] * inv_l);
-                if (row < N) {
-                  uint4* dst = reinterpret_cast<uint4*>(out + c * 32 + 16 * h);
-                  dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
-                  dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
-                }
-              }
-            }
-          }
-        }
+        tail.part_ml[(((size_t)x.tb * 2 + g) * tail.pieces + x.part) * BM + r_local] = make_float2(m_used, l);
       }
       tc_fence_before();
       mbar_arrive(o_free(g));  // the next unit's first P.V may overwrite O now
@@ -738,6 +673,49 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
     tc_fence_after();
     tmem_dealloc(tmem, C::TMEM_COLS);
   }
+}
+
+// Merge of the K/V parts of a launch's tail blocks. Block (tail block, Q tile, 32-column chunk); thread =
+// query row. m = max_p m_p, O = sum_p 2^(m_p - m) O_p / sum_p 2^(m_p - m) l_p, summed over the parts in
+// their fixed order (results do not depend on which part ran first or where).
+template <int D, bool BF16>
+__global__ void __launch_bounds__(BM)
+merge_kv_parts(const float4* __restrict__ part_o, const float2* __restrict__ part_ml, uint16_t* __restrict__ O,
+               int BH, int N, int n_qblk, int group_heads, int tail_from, int P) {
+  const int tb = blockIdx.x, g = blockIdx.y, c = blockIdx.z, r = threadIdx.x;
+  int bh, qt0;
+  block_coords(tail_from + tb, BH, n_qblk, group_heads, &bh, &qt0);
+  const int row = (qt0 + g) * BM + r;
+  if (qt0 + g >= (N + BM - 1) / BM || row >= N) return;  // no second Q tile / past the end
+  const size_t slot0 = ((size_t)tb * 2 + g) * P;
+  float m = -CUDART_INF_F;
+  for (int q = 0; q < P; ++q) m = fmaxf(m, part_ml[(slot0 + q) * BM + r].x);
+  float acc[32], lt = 0.f;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) acc[i] = 0.f;
+  for (int q = 0; q < P; ++q) {
+    const float2 ml = part_ml[(slot0 + q) * BM + r];
+    const float w = ex2(ml.x - m);
+    lt = fmaf(w, ml.y, lt);
+    const float4* po = part_o + (slot0 + q) * (D / 4) * BM + r;
+    float4 v[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = po[(size_t)(c * 8 + i) * BM];  // all eight loads in flight at once
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      acc[4 * i] = fmaf(w, v[i].x, acc[4 * i]);
+      acc[4 * i + 1] = fmaf(w, v[i].y, acc[4 * i + 1]);
+      acc[4 * i + 2] = fmaf(w, v[i].z, acc[4 * i + 2]);
+      acc[4 * i + 3] = fmaf(w, v[i].w, acc[4 * i + 3]);
+    }
+  }
+  const float inv_l = 1.f / lt;
+  uint32_t w[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) w[i] = pack2<BF16>(acc[2 * i] * inv_l, acc[2 * i + 1] * inv_l);
+  uint4* dst = reinterpret_cast<uint4*>(O + ((size_t)bh * N + row) * D + c * 32);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) dst[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
 }
 
 // Failure-path probe: one warp waits, with the same bounded mbarrier wait the attention kernel uses,
@@ -872,13 +850,14 @@ struct Plan {
 
 // K/V parts per tail block: the fewest parts P (2..8, at least kMinPartTiles K/V tiles each) that minimise
 // the tail's length ceil(r*P/G)/P (in units of one block's time), used only if the launch's predicted length
-// falls by at least kMinPartGain: waves + 1 -> waves + that length. The parts cost time of their own (the
-// K/V-part instantiation runs ~2% slower per tile, and each part writes and the last one reads partial
-// results), and the units of earlier waves end at staggered times, so the last wave is less idle than this
-// count says: config 4 on one B200 (13 full waves + 124 of 148 blocks, predicted -1%) measured 2.6% slower
-// with 7 parts, while a launch of 1 full wave + 108 blocks (config 4 on 8 GPUs) is predicted 12.5% faster.
+// falls by at least kMinPartGain: waves + 1 -> waves + that length. The parts cost time of their own (each
+// part restarts the pipeline and writes its partial result, merge_kv_parts reads them all), and units of
+// earlier waves end at staggered times, so the last wave is less idle than this count says. Measured on a
+// B200: config 4 (13 full waves + 124 of 148 blocks, predicted 1%) was 2.6% slower with 7 parts; config 4's
+// 8-GPU shard (1 full wave + 108 blocks, predicted 12.5%) runs 3.6% faster with 4 parts; parts of 8 K/V tiles
+// (config 3's 8-GPU shard) lost 24% with an in-kernel merge, hence at least 16 tiles per part.
 constexpr int kMaxParts = 8;
-constexpr int kMinPartTiles = 4;
+constexpr int kMinPartTiles = 16;
 constexpr double kMinPartGain = 0.08;
 int kv_parts(long long waves, long long r, long long grid, int n_kv) {
   int best = 1;
@@ -966,12 +945,9 @@ struct Scratch {
 };
 
 size_t round256(size_t b) { return (b + 255) & ~size_t(255); }
-// Bytes of the counters (zeroed before each launch) and of the K/V parts' partial results of a plan, 0 when
-// unused; counter_bytes() is the 256-byte-aligned room they take in an allocation.
-size_t counters_used(const Plan& p) {
-  if (!p.uses_counter && !p.tail_kv) return 0;
-  return sizeof(int) * (1 + (p.tail_kv ? (size_t)p.n_tail * 2 * tc::BM : 0));
-}
+// Bytes of the work counter (zeroed before each launch) and of the K/V parts' partial results of a plan, 0
+// when unused; counter_bytes() is the 256-byte-aligned room the counter takes in an allocation.
+size_t counters_used(const Plan& p) { return p.uses_counter ? sizeof(int) : 0; }
 size_t counter_bytes(const Plan& p) { return round256(counters_used(p)); }
 size_t part_o_bytes(const Plan& p, int d) {
   return p.tail_kv ? (size_t)p.n_tail * 2 * p.tail_pieces * tc::BM * d * sizeof(float) : 0;
@@ -999,14 +975,22 @@ cudaError_t launch_t(const LaunchArgs& a, const Plan& p, const CUtensorMap& mq, 
   if ((p.uses_counter && s.ctr == nullptr) || (p.tail_kv && (s.part_o == nullptr || s.part_ml == nullptr)))
     return cudaErrorInvalidValue;
   const float scale_log2 = 1.4426950408889634f / sqrtf((float)D);
-  tc::Tail tail{p.tail_from, p.tail_pieces, p.tail_kv ? 1 : 0, s.part_o, s.part_ml, s.ctr ? s.ctr + 1 : nullptr};
+  tc::Tail tail{p.tail_from, p.tail_pieces, p.tail_kv ? 1 : 0, s.part_o, s.part_ml};
   timing_begin(a.stream);
   kern<<<p.grid, tc::NUM_THREADS, smem, a.stream>>>(mq, mk, mv, mvh, s.flags, static_cast<uint16_t*>(a.o), a.BH,
                                                      a.N, scale_log2, a.causal ? 1 : 0, p.group_heads, tail,
                                                      a.status, s.ctr);
-  timing_end(a.stream);
   note_launch();
-  return cudaGetLastError();
+  cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess && p.tail_kv) {
+    const int n_qblk = ((a.N + tc::BM - 1) / tc::BM + 1) / 2;
+    tc::merge_kv_parts<D, BF16><<<dim3(p.n_tail, 2, D / 32), tc::BM, 0, a.stream>>>(
+        s.part_o, s.part_ml, static_cast<uint16_t*>(a.o), a.BH, a.N, n_qblk, p.group_heads, p.tail_from, p.tail_pieces);
+    note_launch();
+    e = cudaGetLastError();
+  }
+  timing_end(a.stream);
+  return e;
 }
 
 // One call in the scratch `s`: zero the counters, stage V as fp16 (bf16), run the attention kernel.

@@ -245,7 +245,8 @@ def profile(cmd: list[str], kernel_regex: str = "attn_fwd_tc|stage_v_f16", skip:
 
 def summary_markdown(res: dict, cmd: list[str], flops, nbytes, peaks: dict) -> str:
     lines = [f"# ncu counters via `cuda_attn.hw_counters`", "",
-             "Produced by (run from the repository root, after the same command exited 0 without ncu):", "",
+             f"Produced by (run in `{os.path.basename(os.getcwd())}/`, after the same command exited 0 without "
+             "ncu):", "",
              "```", "python -m cuda_attn.hw_counters " + " ".join(sys.argv[1:]), "```", "",
              "which ran:", "", "```", res.get("command", ""), "```", ""]
     groups = calls(res["launches"])
