@@ -25,8 +25,9 @@ How it works, in three steps that can run on different machines:
   3. read     the report with Nsight Compute's own Python reader (ncu_report, shipped with ncu under
               extras/python), in ncu's base units: time in ns, bytes, percent.
 
-A call of the bf16 path is two launches (stage_v_f16, then attn_fwd_tc): `calls()` groups each run of
-launches that ends with the attention kernel into one call, and `aggregate()` combines it.
+A call of the bf16 path is two launches (stage_v_f16, then attn_fwd_tc), and a call whose last wave runs
+as K/V parts adds merge_kv_parts: `calls()` groups the launches of each call, and `aggregate()` combines
+them.
 
     python -m cuda_attn.hw_counters --flops 4.398e12 --bytes 536870912 --out profiles/x.md -- \
         python bench.py --config config4 --steps 1 --warmup 1 --no-cpu-baseline
@@ -148,11 +149,18 @@ def read_report(path: str, metrics: list[str], reader=None) -> list[dict]:
     return out
 
 
+MERGE_KERNEL = "merge_kv_parts"
+
+
 def calls(launches: list[dict], last: str = ATTENTION_KERNEL) -> list[list[dict]]:
     """Group launches into forward calls: each group ends with a launch of the attention kernel (a bf16
-    call is stage_v_f16 then attn_fwd_tc). Launches after the last attention kernel form no call."""
+    call is stage_v_f16 then attn_fwd_tc), plus the merge_kv_parts launch that follows it when the call
+    cut its last wave into K/V parts. Launches after the last attention kernel form no call."""
     groups, cur = [], []
     for rec in launches:
+        if MERGE_KERNEL in rec["kernel"] and groups and not cur:
+            groups[-1].append(rec)
+            continue
         cur.append(rec)
         if last in rec["kernel"]:
             groups.append(cur)
@@ -218,7 +226,7 @@ def roofline(rec: dict, flops: float | None = None, algorithmic_bytes: float | N
     return out
 
 
-def profile(cmd: list[str], kernel_regex: str = "attn_fwd_tc|stage_v_f16", skip: int = 0, count: int = 2,
+def profile(cmd: list[str], kernel_regex: str = "attn_fwd_tc|stage_v_f16|merge_kv_parts", skip: int = 0, count: int = 2,
             report: str | None = None, chip: str = "gb100", timeout: int = 900) -> dict:
     """check -> capture -> read for `cmd`. Returns {'status', 'launches', 'unobservable', 'report', 'log'};
     status ok | no_ncu | no_permission | no_reader | error."""
@@ -265,7 +273,7 @@ def summary_markdown(res: dict, cmd: list[str], flops, nbytes, peaks: dict) -> s
 
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
-    ap.add_argument("--kernel", default="attn_fwd_tc|stage_v_f16", help="ncu -k regex")
+    ap.add_argument("--kernel", default="attn_fwd_tc|stage_v_f16|merge_kv_parts", help="ncu -k regex")
     ap.add_argument("--skip", type=int, default=0, help="matching launches to skip (ncu -s)")
     ap.add_argument("--count", type=int, default=2, help="matching launches to profile (ncu -c)")
     ap.add_argument("--flops", type=float, default=None, help="algorithmic FLOPs of one call")

@@ -97,6 +97,12 @@ def test_calls_group_staging_with_the_attention_kernel():
     assert [[r[T] for r in g] for g in groups] == [[1, 2], [3]]
 
 
+def test_calls_attach_the_merge_of_k_v_parts():
+    ls = [launch("tc::stage_v_f16", 1), launch("tc::attn_fwd_tc<128, true, true>", 2),
+          launch("tc::merge_kv_parts<128, true>", 3), launch("tc::attn_fwd_tc<128, false, false>", 4)]
+    assert [[r[T] for r in g] for g in hc.calls(ls)] == [[1, 2, 3], [4]]
+
+
 def test_aggregate_sums_weights_and_takes_the_longest():
     g = [launch("tc::stage_v_f16", 1.0e5, tensor=0.0, rd=1.0e8, wr=1.0e8, regs=38),
          launch("tc::attn_fwd_tc", 3.0e6, tensor=70.0, rd=4.0e8, wr=1.2e8, regs=168)]
