@@ -116,7 +116,7 @@ def test_torch_binding_signatures():
 @pytest.mark.parametrize("bh,chunks", [(32, 8), (128, 8), (10, 3), (10, 1), (1, 8), (7, 8), (5, 3), (2, 8), (1000, 7)])
 def test_host_pipeline_chunk_plan(bh, chunks):
     """fused_tc_host's chunk plan covers every head once: full chunks, then the last one cut into halves
-    down to one head (a short tail after the last input copy); one chunk when chunks <= 1."""
+    down to chunks of two heads (a short tail after the last input copy); one chunk when chunks <= 1."""
     from cuda_attn.pipeline import chunk_plan
     sizes = chunk_plan(bh, chunks)
     assert sum(sizes) == bh and min(sizes) >= 1
@@ -127,5 +127,4 @@ def test_host_pipeline_chunk_plan(bh, chunks):
     assert per == -(-bh // chunks)
     assert all(s <= per for s in sizes)
     assert sizes == sorted(sizes, reverse=True)
-    if bh > 1:
-        assert sizes[-1] == 1
+    assert sizes[-1] <= 3  # halving stops once fewer than four heads are left

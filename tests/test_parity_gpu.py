@@ -290,6 +290,26 @@ def test_two_threads_through_the_host_pipeline(capi):
         assert torch.equal(results[i], expect[i]), f"thread {i} differs from the device-resident call"
 
 
+def test_host_pipeline_chained_calls_without_synchronising(capi):
+    """Back-to-back host calls overlap (the next call's input copies start at once); a call whose input is
+    an earlier call's output still being copied back waits for that copy: chaining two layers (O of the
+    first as Q of the second) with synchronize=False equals the device-resident chain bit for bit."""
+    import cuda_attn
+    q, k, v = make_qkv(1, 12, 2048, 128, torch.bfloat16, seed=41)
+    o1 = torch.empty_like(q)
+    capi.fused_tc(q, k, v, o1)
+    o2 = torch.empty_like(q)
+    capi.fused_tc(o1, k, v, o2)
+    hq, hk, hv = (x.cpu().pin_memory() for x in (q, k, v))
+    h1 = torch.empty(q.shape, dtype=q.dtype, pin_memory=True)
+    h2 = torch.empty(q.shape, dtype=q.dtype, pin_memory=True)
+    for _ in range(2):
+        cuda_attn.fused_tc_host(hq, hk, hv, out=h1, chunks=4, synchronize=False)
+        cuda_attn.fused_tc_host(h1, hk, hv, out=h2, chunks=4, synchronize=False)
+    torch.cuda.synchronize()
+    assert torch.equal(h1, o1.cpu()) and torch.equal(h2, o2.cpu())
+
+
 def test_reruns_are_bit_identical(capi):
     q, k, v = make_qkv(2, 4, 1500, 128, torch.bfloat16, seed=8)
     a = run_capi(capi, "fused_tc", q, k, v, True)
