@@ -540,6 +540,7 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
     const uint32_t t_s = tmem + lane_off + (g ? C::T_S1 : C::T_S0);
     const uint32_t t_p = tmem + lane_off + (g ? C::T_P1 : C::T_P0);
     const uint32_t t_o = tmem + lane_off + (g ? C::T_O1 : C::T_O0);
+    const bool o_align32 = (reinterpret_cast<uintptr_t>(O) & 31) == 0;
     int sc = 0, oc = 0;  // S products read and P.V products waited for, this Q tile, all units
     bool ok = true;
     for (int nu = 0;; ++nu) {
@@ -642,9 +643,16 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
           for (int i = 0; i < 16; ++i)
             w[i] = pack2<BF16>(__uint_as_float(rr[2 * i]) * inv_l, __uint_as_float(rr[2 * i + 1]) * inv_l);
           if (row < N) {
-            uint4* dst = reinterpret_cast<uint4*>(out + c * 32);
+            // 64 bytes of the row: two 32-byte stores (measured +0.2% to +3% over 16-byte ones) when O is
+            // 32-byte aligned (every row and chunk offset then is), else four 16-byte stores
+            if (o_align32) {
+              st_global_v8(out + c * 32, w);
+              st_global_v8(out + c * 32 + 16, w + 8);
+            } else {
+              uint4* dst = reinterpret_cast<uint4*>(out + c * 32);
 #pragma unroll
-            for (int i = 0; i < 4; ++i) dst[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+              for (int i = 0; i < 4; ++i) dst[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+            }
           }
         }
       } else if constexpr (KV_PARTS) {
@@ -713,9 +721,15 @@ merge_kv_parts(const float4* __restrict__ part_o, const float2* __restrict__ par
   uint32_t w[16];
 #pragma unroll
   for (int i = 0; i < 16; ++i) w[i] = pack2<BF16>(acc[2 * i] * inv_l, acc[2 * i + 1] * inv_l);
-  uint4* dst = reinterpret_cast<uint4*>(O + ((size_t)bh * N + row) * D + c * 32);
+  uint16_t* dst = O + ((size_t)bh * N + row) * D + c * 32;
+  if ((reinterpret_cast<uintptr_t>(O) & 31) == 0) {
+    st_global_v8(dst, w);
+    st_global_v8(dst + 16, w + 8);
+  } else {
+    uint4* d4 = reinterpret_cast<uint4*>(dst);
 #pragma unroll
-  for (int i = 0; i < 4; ++i) dst[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+    for (int i = 0; i < 4; ++i) d4[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+  }
 }
 
 // Failure-path probe: one warp waits, with the same bounded mbarrier wait the attention kernel uses,

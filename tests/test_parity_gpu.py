@@ -221,6 +221,23 @@ def test_kv_parts_switch_rejects_other_values(capi):
     assert capi.get_kv_parts() is True
 
 
+@pytest.mark.parametrize("d", [64, 128])
+def test_output_16_byte_but_not_32_byte_aligned(capi, d):
+    """The C ABI accepts any 16-byte-aligned O; the epilogue's 32-byte stores are used only when O is
+    32-byte aligned, so an output that starts 16 bytes into an allocation is written correctly too (with
+    K/V parts as well: 4 heads at N = 16384 cut the tail on a B200)."""
+    for bh, n in ((3, 1000), (4, 16384 if d == 128 else 4096)):
+        q, k, v = make_qkv(1, bh, n, d, torch.bfloat16, scale=0.5, seed=bh + d)
+        base = torch.full((q.numel() + 16,), float("nan"), dtype=q.dtype, device=q.device)
+        o = base[8:8 + q.numel()].view(q.shape)  # 8 bf16 = 16 bytes past a 256-byte-aligned start
+        assert o.data_ptr() % 32 == 16
+        capi.fused_tc(q, k, v, o)
+        o_ref = torch.empty_like(q)
+        capi.fused_tc(q, k, v, o_ref)
+        torch.cuda.synchronize()
+        assert torch.equal(o, o_ref), (bh, n)
+
+
 def test_non_default_stream(capi):
     q, k, v = make_qkv(1, 4, 777, 128, torch.bfloat16, seed=3)
     s = torch.cuda.Stream()
