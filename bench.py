@@ -357,6 +357,20 @@ def main():
         dist.broadcast(t, src=0)
         gate_ok = bool(t.item() > 0.5)
 
+    # peak device memory of one call through the torch API (reference bench/benchmark.py:96-102 records
+    # peak_memory_mb): torch's allocation (O) plus the library's per-launch scratch high-water mark
+    torch.cuda.synchronize()
+    torch.cuda.reset_peak_memory_stats(dev)
+    mem_base = torch.cuda.memory_allocated(dev)
+    capi.scratch_bytes(reset=True)
+    o_api = cuda_attn.fused_tc(q, k, v, job.causal)
+    torch.cuda.synchronize()
+    scratch_hw, scratch_reserved = capi.scratch_bytes()
+    peak_mem = {"torch_mb": (torch.cuda.max_memory_allocated(dev) - mem_base) / 2**20,
+                "library_scratch_mb": scratch_hw / 2**20, "library_pool_reserved_mb": scratch_reserved / 2**20}
+    peak_mem["peak_memory_mb"] = peak_mem["torch_mb"] + peak_mem["library_scratch_mb"]
+    del o_api
+
     def step():
         capi.fused_tc(q, k, v, o, causal=job.causal, stream=stream)
 
@@ -494,6 +508,9 @@ def main():
         "e2e": {"value": total_flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms, "steps": e2e_steps,
                 "path": "pinned host -> cuda_attn.fused_tc_host (public API; copies overlapped with the kernel over head chunks: 8 full, the last cut in halves) -> pinned host", "matches_value_run": e2e_same},
+        "memory": dict(peak_mem, inputs_mb=3 * q.numel() * q.element_size() / 2**20,
+                       note="one cuda_attn.fused_tc call on this rank's heads: O from torch plus the library's "
+                            "scratch (bf16: fp16 copy of V; multi-wave: work counter; K/V parts: partials)"),
         "gpu_launches": launches,
         "kernel_launches_timed": kernel_launches,
         "clocks": clocks,

@@ -1139,6 +1139,28 @@ cudaError_t launch_fused_tc_sm100(const LaunchArgs& a) {
   return a.d == 64 ? launch_alloc<64>(a, mq, mk, mv, dev) : launch_alloc<128>(a, mq, mk, mv, dev);
 }
 
+cudaError_t scratch_usage(int dev, long long* high_water, long long* reserved, bool reset) {
+  *high_water = 0;
+  *reserved = 0;
+  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  cudaMemPool_t pool = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(g_pool_mu);
+    pool = g_pool[dev];
+  }
+  if (pool == nullptr) return cudaSuccess;  // no call on this device has needed scratch yet
+  uint64_t hw = 0, rs = 0;
+  cudaError_t e = cudaMemPoolGetAttribute(pool, cudaMemPoolAttrUsedMemHigh, &hw);
+  if (e == cudaSuccess) e = cudaMemPoolGetAttribute(pool, cudaMemPoolAttrReservedMemCurrent, &rs);
+  if (e == cudaSuccess && reset) {
+    uint64_t zero = 0;
+    e = cudaMemPoolSetAttribute(pool, cudaMemPoolAttrUsedMemHigh, &zero);
+  }
+  *high_water = (long long)hw;
+  *reserved = (long long)rs;
+  return e;
+}
+
 cudaError_t launch_wait_expiry_probe(int* status, int* status2, cudaStream_t stream) {
   tc::wait_expiry_probe<<<1, 32, 0, stream>>>(status, status2);
   note_launch();

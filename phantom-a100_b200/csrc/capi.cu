@@ -414,6 +414,16 @@ int phantom_attn_set_kv_parts(int allow) {
 
 int phantom_attn_get_kv_parts(void) { return g_shape.kv_parts; }
 
+int phantom_attn_scratch_bytes(long long* high_water, long long* reserved, int reset) {
+  if (!high_water || !reserved) return fail(PHANTOM_ATTN_ERR_INVALID, "scratch_bytes: null output pointer");
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e == cudaSuccess) e = scratch_usage(dev, high_water, reserved, reset != 0);
+  if (e != cudaSuccess) return cuda_fail("scratch_bytes", e);
+  g_last_error.clear();
+  return PHANTOM_ATTN_OK;
+}
+
 long long phantom_attn_launch_count(int reset) {
   const long long n = g_launches;
   if (reset) g_launches = 0;

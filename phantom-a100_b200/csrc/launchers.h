@@ -35,6 +35,10 @@ cudaError_t launch_fused_simt(const LaunchArgs& a);
 cudaError_t launch_wait_expiry_probe(int* status, int* status2, cudaStream_t stream);
 size_t fused_simt_smem_bytes(int d);
 
+// High-water mark of the scratch taken from device `dev`'s memory pool since the last reset, and the bytes
+// the pool holds now (both 0 before any call needed scratch); reset = true restarts the high-water mark.
+cudaError_t scratch_usage(int dev, long long* high_water, long long* reserved, bool reset);
+
 // Number of kernel launches the library has made on this thread (benchmark accounting).
 void note_launch();
 

@@ -36,6 +36,7 @@ SIGNATURES = {
     "phantom_attn_kernel_timing_read": (_I, [ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_longlong)]),
     "phantom_attn_set_launch_shape": (_I, [ctypes.c_longlong, _I]),
     "phantom_attn_get_launch_shape": (_I, [ctypes.POINTER(ctypes.c_longlong), ctypes.POINTER(_I)]),
+    "phantom_attn_scratch_bytes": (_I, [ctypes.POINTER(ctypes.c_longlong), ctypes.POINTER(ctypes.c_longlong), _I]),
     "phantom_attn_set_kv_parts": (_I, [_I]),
     "phantom_attn_get_kv_parts": (_I, []),
 }
@@ -128,6 +129,13 @@ class CAPI:
         """Launch the kernel whose bounded wait must expire (about a second); device_status() then
         reports STATUS_PROBE."""
         self._check(self.lib.phantom_attn_wait_expiry_probe(self._stream(stream)))
+
+    def scratch_bytes(self, reset: bool = False) -> tuple[int, int]:
+        """(high-water bytes of the library's per-launch scratch on the current device since the last reset,
+        bytes its pool holds now)."""
+        hw, rs = ctypes.c_longlong(0), ctypes.c_longlong(0)
+        self._check(self.lib.phantom_attn_scratch_bytes(ctypes.byref(hw), ctypes.byref(rs), int(bool(reset))))
+        return hw.value, rs.value
 
     def launch_count(self, reset: bool = False) -> int:
         return int(self.lib.phantom_attn_launch_count(int(reset)))

@@ -82,7 +82,7 @@ def chunk_plan(bh: int, chunks: int) -> list[int]:
 
 def fused_tc_host(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool = False,
                   out: torch.Tensor | None = None, chunks: int = 8, device: int | torch.device | None = None,
-                  synchronize: bool = True) -> torch.Tensor:
+                  synchronize: bool = True, trace: list | None = None) -> torch.Tensor:
     """fused_tc for (B, H, N, d) CPU tensors (pin them for overlap; pageable memory works but serialises
     the copies). Returns O as a CPU tensor of the input dtype (`out` if given, pinned otherwise). With
     synchronize=False the call returns once the work is queued; the current CUDA stream of `device` is
@@ -93,7 +93,10 @@ def fused_tc_host(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: boo
     their values when the call is made; the one exception it tracks is an output of an earlier call on
     this thread that is still being copied back, which the input copies wait for (chained calls, e.g.
     one call's O as the next call's Q). The output copies wait for the current stream, so GPU work queued
-    on it before the call that still reads `out` is not overwritten."""
+    on it before the call that still reads `out` is not overwritten.
+
+    trace: if a list is given, one record per chunk is appended - {"heads", "h2d", "attend", "d2h"}, each
+    a (start, end) pair of CUDA events (timing-enabled) on that stage's stream (cuda_attn.timeline)."""
     for t in (q, k, v):
         if t.is_cuda:
             raise RuntimeError("fused_tc_host: inputs must be CPU tensors (use fused_tc for device tensors)")
@@ -118,12 +121,20 @@ def fused_tc_host(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: boo
     kv_parts = lib.get_kv_parts()
     lib.set_kv_parts(False)
     try:
-        return _pipeline(lib, hq, hk, hv, ho, out, sizes, per, n_slots, N, d, q.dtype, causal, dev, synchronize)
+        return _pipeline(lib, hq, hk, hv, ho, out, sizes, per, n_slots, N, d, q.dtype, causal, dev, synchronize,
+                         trace)
     finally:
         lib.set_kv_parts(kv_parts)
 
 
-def _pipeline(lib, hq, hk, hv, ho, out, sizes, per, n_slots, N, d, dtype, causal, dev, synchronize):
+def _pipeline(lib, hq, hk, hv, ho, out, sizes, per, n_slots, N, d, dtype, causal, dev, synchronize, trace=None):
+    def mark(stream):
+        if trace is None:
+            return None
+        e = torch.cuda.Event(enable_timing=True)
+        e.record(stream)
+        return e
+
     with torch.cuda.device(dev):
         h2d, comp, d2h = _streams(dev)
         cur = torch.cuda.current_stream(dev)
@@ -147,18 +158,26 @@ def _pipeline(lib, hq, hk, hv, ho, out, sizes, per, n_slots, N, d, dtype, causal
             if i >= n_slots:
                 h2d.wait_event(freed[s])
             with torch.cuda.stream(h2d):
+                t0 = mark(h2d)
                 dq.copy_(hq[a:b], non_blocking=True)
                 dk.copy_(hk[a:b], non_blocking=True)
                 dv.copy_(hv[a:b], non_blocking=True)
+                t1 = mark(h2d)
                 loaded[s].record(h2d)
             comp.wait_event(loaded[s])
+            t2 = mark(comp)
             lib.fused_tc(dq.unsqueeze(0), dk.unsqueeze(0), dv.unsqueeze(0), do.unsqueeze(0), causal=causal,
                          stream=comp)
+            t3 = mark(comp)
             computed[s].record(comp)
             d2h.wait_event(computed[s])
             with torch.cuda.stream(d2h):
+                t4 = mark(d2h)
                 ho[a:b].copy_(do, non_blocking=True)
+                t5 = mark(d2h)
                 freed[s].record(d2h)
+            if trace is not None:
+                trace.append({"heads": n, "h2d": (t0, t1), "attend": (t2, t3), "d2h": (t4, t5)})
         cur.wait_stream(d2h)
         done = torch.cuda.Event()
         done.record(d2h)

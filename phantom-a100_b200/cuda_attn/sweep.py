@@ -68,6 +68,23 @@ def time_cuda(fn, warmup, iters, flush_buf):
     return float(np.median(ms)), float(np.percentile(ms, 10)), float(np.percentile(ms, 90))
 
 
+def peak_memory_mb(fn, lib=None):
+    """Device memory one call takes beyond what was allocated before it (reference bench/benchmark.py:96-102):
+    torch's peak allocation delta plus, for this library's kernels, its per-launch scratch high-water mark
+    (the scratch comes from the library's own memory pool, which torch does not see)."""
+    torch.cuda.synchronize()
+    torch.cuda.reset_peak_memory_stats()
+    base = torch.cuda.memory_allocated()
+    if lib is not None:
+        lib.scratch_bytes(reset=True)
+    fn()
+    torch.cuda.synchronize()
+    mb = (torch.cuda.max_memory_allocated() - base) / 2**20
+    if lib is not None:
+        mb += lib.scratch_bytes()[0] / 2**20
+    return mb
+
+
 def check(out, ref, dtype):
     out, ref = out.double(), ref.double()
     if dtype == torch.float32:
@@ -101,7 +118,10 @@ def main(argv=None):
     meta = dict(gpu=torch.cuda.get_device_name(), cc="sm_%d%d" % torch.cuda.get_device_capability(),
                 torch=torch.__version__, timestamp=datetime.now(timezone.utc).isoformat(timespec="seconds"))
     fields = ["gpu", "cc", "torch", "timestamp", "impl", "dtype", "causal", "B", "H", "N", "d", "median_ms", "p10_ms",
-              "p90_ms", "tflops", "hbm_gbs", "frac_bf16_sustained", "frac_hbm", "regime", "err", "status"]
+              "p90_ms", "tflops", "hbm_gbs", "frac_bf16_sustained", "frac_hbm", "regime", "peak_memory_mb", "err",
+              "status"]
+    from .capi import CAPI
+    lib = CAPI()
     causal_modes = {"off": [False], "on": [True], "both": [False, True]}[a.causal]
     with open(a.out, "w", newline="") as fh:
         w = csv.DictWriter(fh, fieldnames=fields)
@@ -131,6 +151,7 @@ def main(argv=None):
                             else:
                                 err = float("nan")
                             med, p10, p90 = time_cuda(fn, a.warmup, a.iters, flush)
+                            mem = peak_memory_mb(fn, lib if name in TENSOR_CORE else None)
                         except torch.cuda.OutOfMemoryError:
                             torch.cuda.empty_cache()
                             w.writerow(dict(row, status="oom"))
@@ -140,7 +161,8 @@ def main(argv=None):
                         w.writerow(dict(row, median_ms=f"{med:.4f}", p10_ms=f"{p10:.4f}", p90_ms=f"{p90:.4f}",
                                         tflops=f"{tf:.2f}", hbm_gbs=f"{gbs:.1f}",
                                         frac_bf16_sustained=f"{tf / peaks['bf16_tflops_sustained']:.3f}",
-                                        frac_hbm=f"{gbs / peaks['hbm_gbs']:.3f}", err=f"{err:.2e}", status="ok"))
+                                        frac_hbm=f"{gbs / peaks['hbm_gbs']:.3f}", peak_memory_mb=f"{mem:.3f}",
+                                        err=f"{err:.2e}", status="ok"))
                         fh.flush()
                         print(f"causal={causal!s:5} d={d:3} N={n:5} {name:20} {med:8.4f} ms {tf:8.1f} TFLOP/s "
                               f"{gbs:8.1f} GB/s [{regime}] err={err:.1e}", flush=True)

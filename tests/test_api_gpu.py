@@ -141,3 +141,42 @@ def test_sweep_tool_writes_gated_rows(tmp_path):
                        "--impls", "fused_tc", "fused", "--out", str(out)]) == 0
     rows = list(csv.DictReader(open(out)))
     assert len(rows) == 8 and all(r["status"] == "ok" for r in rows), rows
+    # peak memory of one call: at least O (B*H*N*d fp16 elements; the sweep's default dtype)
+    for r in rows:
+        o_mb = 4 * int(r["N"]) * int(r["d"]) * 2 / 2**20
+        assert float(r["peak_memory_mb"]) >= o_mb - 1e-3, r
+
+
+def test_scratch_bytes_report_the_pool_high_water_mark():
+    """phantom_attn_scratch_bytes: a bf16 call takes the fp16 copy of V (2*B*H*N*d bytes) plus flags and, when
+    its launch has several waves, the work counter from the library pool; the high-water mark covers that
+    and restarts on reset; a one-wave fp16 call takes no scratch."""
+    from cuda_attn.capi import CAPI
+    lib = CAPI()
+    q = torch.randn(1, 8, 2048, 128, device="cuda").to(torch.bfloat16)
+    o = torch.empty_like(q)
+    lib.fused_tc(q, q, q, o)
+    torch.cuda.synchronize()
+    lib.scratch_bytes(reset=True)
+    lib.fused_tc(q, q, q, o)
+    torch.cuda.synchronize()
+    hw, reserved = lib.scratch_bytes(reset=True)
+    assert hw >= 2 * q.numel() and reserved >= hw, (hw, reserved)
+    h = torch.randn(1, 2, 256, 64, device="cuda").half()
+    lib.fused_tc(h, h, h, torch.empty_like(h))
+    torch.cuda.synchronize()
+    assert lib.scratch_bytes()[0] == 0
+
+
+def test_run_one_and_timeline_tools():
+    """cuda_attn.run_one (a fixed profiling target) runs; cuda_attn.timeline orders every chunk's stages
+    (input copy, attention, output copy) and accounts for every head of every call."""
+    from cuda_attn import run_one, timeline
+    assert run_one.main(["--impl", "fused_tc", "--n", "512", "--dim", "128", "--dtype", "bf16", "--reps", "2"]) == 0
+    summary, rows = timeline.run("config2", chunks=4, calls=2, warmup=1)
+    assert summary["ms_per_call"] > 0 and summary["h2d_gbs_while_busy"] > 1
+    from cuda_attn.workloads import CONFIGS
+    assert sum(r["heads"] for r in rows) == 2 * CONFIGS["config2"].BH
+    for r in rows:
+        assert r["h2d"][0] <= r["h2d"][1] <= r["attend"][0] + 1e-3
+        assert r["attend"][0] <= r["attend"][1] <= r["d2h"][0] + 1e-3 and r["d2h"][0] <= r["d2h"][1]
