@@ -66,7 +66,7 @@ constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale O only when th
 
 // Status-word bits (which wait expired).
 constexpr int kErrTmaWait = 1, kErrMmaWait = 2, kErrSoftmaxWait = 4, kErrEpilogueWait = 8;
-constexpr int kUnitRing = 4;  // published work-unit ids (shared memory)
+constexpr int kUnitRing = 4;  // published work units (shared memory, 32 bytes each)
 
 // TMEM plan per head dimension (K/V tiles of BN = 128 keys). P (the probabilities as packed 16-bit
 // pairs, the A operand of O += P V) never shares columns with S (fp32 scores), so a Q.K^T product is
@@ -92,8 +92,14 @@ struct Cfg {
   // barriers: q_full, kv_full[STAGES], kv_empty[STAGES], s_full[2], s_free[2], p_ready[2], o_done[2],
   // drain (S issuer), drain (P.V issuer), q_free, o_free[2]
   static constexpr int NUM_BARS = 1 + 2 * STAGES + 13;
-  static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;  // TMEM base address, abort flag
-  static constexpr int SMEM_BYTES = OFF_MISC + 16 + 16 + 1024;  // + unit-id ring, + slack to align to 1024
+  static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;  // TMEM base address, abort flag, unit ring
+  // O staging for the TMA-store epilogue: per softmax warp one 32-row x 64-column 16-bit block (4 KB) in the
+  // 128-byte swizzled layout of the output tensor map (1024-byte aligned)
+  static constexpr int OST_WARP = 32 * 128;
+  static constexpr int OFF_OST = (OFF_MISC + 16 + 32 * kUnitRing + 1023) / 1024 * 1024;
+  static constexpr int SMEM_BYTES = OFF_OST + 8 * OST_WARP + 1024;  // + slack to align the base to 1024
+  static_assert(SMEM_BYTES <= 227 * 1024, "shared memory plan exceeds 227 KB");
+  static_assert((OFF_MISC + 16) % 16 == 0, "unit ring must be 16-byte aligned");
   static constexpr uint32_t TMEM_COLS = 512;
   static constexpr uint32_t T_S0 = SHARED_S ? 0 : 2 * D, T_S1 = SHARED_S ? 0 : 2 * D + BN;
   static constexpr uint32_t T_P0 = SHARED_S ? BN : 2 * D + 2 * BN, T_P1 = T_P0 + BN / 2;
@@ -223,7 +229,8 @@ template <int D, bool BF16, bool KV_PARTS>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
 attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
             const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmVh,
-            const int* __restrict__ vflags, uint16_t* __restrict__ O, int BH, int N, float scale_log2, int causal,
+            const __grid_constant__ CUtensorMap tmO, const int* __restrict__ vflags, uint16_t* __restrict__ O,
+            int BH, int N, float scale_log2, int causal,
             int group_heads, const Tail tail, int* __restrict__ status, int* __restrict__ work_ctr) {
   using C = Cfg<D>;
   constexpr int BN = C::BN;
@@ -244,17 +251,17 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
   auto o_free = [&](int g) { return bar0 + 8u * (12 + 2 * C::STAGES + g); };
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 4);
-  volatile int* unit_ring = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 16);  // [kUnitRing]
+  int4* unit_ring = reinterpret_cast<int4*>(smem + C::OFF_MISC + 16);  // [kUnitRing][2]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // Work units: (head, query block of two 128-row Q tiles). Unit order: heads in groups of group_heads
   // whose K and V fit in L2 together; inside a group, the query blocks of all its heads from the
   // heaviest (causal: the most K/V tiles) to the lightest. CTA c starts with unit c; each further unit
-  // is the next one in that order, taken with an atomic counter when the CTA is ready for it, so SMs
-  // that run faster take more units (list scheduling, longest first). The producer warp takes the
-  // units and publishes each id in a shared-memory ring before arriving on q_full; the other roles
-  // read it after their wait on q_full (they are at most one unit behind, so neither the phase nor the
-  // ring slot can be overtaken). An id of -1 ends every role's loop.
+  // is the next one in that order, taken with an atomic counter once the CTA has queued the copies of
+  // its current unit, so SMs that run faster take more units (list scheduling, longest first). The
+  // producer warp takes the units and publishes each (decoded) in a shared-memory ring before arriving
+  // on q_full; the other roles read it after their wait on q_full (they are at most one unit behind, so
+  // neither the phase nor the ring slot can be overtaken). A unit id of -1 ends every role's loop.
   // Query blocks from tail.from on (host-chosen, all two-tile) run as tail.pieces units each: one-tile
   // units, so that a last partial wave of r <= #CTAs/2 blocks becomes 2r short units, one per CTA; or
   // parts of the K/V range, so that a last wave of r > #CTAs/2 blocks spreads over all CTAs.
@@ -264,10 +271,12 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
   struct Unit {
     int bh, row0, kv0, n_kv;
     int part, tb;  // K/V part of a tail block (-1: the whole K/V range), tail block index
-    bool has_b;
+    int has_b;     // the unit has a second Q tile
+    int id;        // unit index; -1 ends the roles' loops
   };
   auto unit_of = [&](int u) {
     Unit x;
+    x.id = u;
     const bool in_tail = u >= tail.from;
     int blk, piece;
     if constexpr (KV_PARTS) {
@@ -341,42 +350,55 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   asm volatile("griddepcontrol.wait;" ::: "memory");
 
-  // Next unit id for a consumer role: wait for the unit's q_full phase, read the published id.
-  auto next_unit = [&](int nu, bool& ok) -> int {
+  // The producer decodes each unit once and publishes it (32 bytes) in the ring; the consumer roles read it
+  // after their wait on q_full instead of decoding the id themselves (three integer divisions each).
+  auto publish_unit = [&](int slot, const Unit& x) {
+    unit_ring[2 * slot] = make_int4(x.bh, x.row0, x.kv0, x.n_kv);
+    unit_ring[2 * slot + 1] = make_int4(x.part, x.tb, x.has_b, x.id);
+  };
+  auto read_unit = [&](int slot) {
+    const int4 a = unit_ring[2 * slot], b = unit_ring[2 * slot + 1];
+    Unit x;
+    x.bh = a.x, x.row0 = a.y, x.kv0 = a.z, x.n_kv = a.w;
+    x.part = b.x, x.tb = b.y, x.has_b = b.z, x.id = b.w;
+    return x;
+  };
+  // Next unit of a consumer role: wait for the unit's q_full phase, read the published unit (id -1: none).
+  auto next_unit = [&](int nu, bool& ok) -> Unit {
     ok = __all_sync(0xffffffffu, mbar_wait(q_full(), nu & 1, abort_flag, status, kErrMmaWait));
-    return ok ? unit_ring[nu % kUnitRing] : -1;
+    if (ok) return read_unit(nu % kUnitRing);
+    Unit x;
+    x.id = -1;
+    return x;
   };
 
   if (warp == TMA_WARP || warp == PV_WARP + 1) {
     setmaxnreg_dec<kRegsProducer>();
     if (warp == TMA_WARP) {
-      // Producer, per unit: take the unit, wait until the previous unit's last Q.K^T has read the Q
-      // buffer, publish the id, load the unit's Q tiles, then K_0, V_0, K_1, V_1, ... into the ring
-      // (warp-uniform loop, one elected lane issues copies).
+      // Producer, per unit: wait until the previous unit's last Q.K^T has read the Q buffer, publish the
+      // unit, load its Q tiles, then K_0, V_0, K_1, V_1, ... into the ring (warp-uniform loop, one elected
+      // lane issues copies), then reserve the next unit.
       int t = 0, nu = 0, nq_arrivals = 0;  // K/V copies, units issued, q_full phases started (+ end marker)
+      int next_u = blockIdx.x;             // the unit this CTA runs next
       bool ok = true;
       if (elect_one()) {
         tma_prefetch_desc(&tmQ);
         tma_prefetch_desc(&tmK);
         tma_prefetch_desc(BF16 ? &tmVh : &tmV);
+        tma_prefetch_desc(&tmO);
       }
       __syncwarp();
       for (;;) {
         if (nu > 0 && !(ok = __all_sync(0xffffffffu, mbar_wait(q_free(), (nu - 1) & 1, abort_flag, status, kErrTmaWait))))
           break;
-        int u = blockIdx.x;
-        if (nu > 0 && n_units <= (int)gridDim.x) {
-          u = n_units;  // one wave: every unit was some CTA's first, the counter is not used
-        } else if (nu > 0) {
-          int got = 0;
-          if (lane == 0) got = (int)gridDim.x + atomicAdd(work_ctr, 1);
-          u = __shfl_sync(0xffffffffu, got, 0);
-        }
-        if (u >= n_units) u = -1;
+        const int u = next_u < n_units ? next_u : -1;
         if (u < 0) {
           if (elect_one()) {
-            unit_ring[nu % kUnitRing] = -1;
-            mbar_arrive(q_full());  // release semantics: the consumers' wait sees the id
+            Unit end;
+            end.bh = end.row0 = end.kv0 = end.n_kv = end.part = end.tb = end.has_b = 0;
+            end.id = -1;
+            publish_unit(nu % kUnitRing, end);
+            mbar_arrive(q_full());  // release semantics: the consumers' wait sees the unit
           }
           __syncwarp();
           ++nq_arrivals;
@@ -386,7 +408,7 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
         const CUtensorMap* tm_v = (BF16 && !head_pv_bf16(x.bh)) ? &tmVh : &tmV;
         const int nq = x.has_b ? 2 : 1;
         if (elect_one()) {
-          unit_ring[nu % kUnitRing] = u;
+          publish_unit(nu % kUnitRing, x);
           mbar_arrive_expect_tx(q_full(), nq * C::Q_TILE);
           for (int g = 0; g < nq; ++g)
             for (int c = 0; c < C::KBLK; ++c)
@@ -407,6 +429,19 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
                           (x.kv0 + (jt >> 1)) * BN, x.bh);
           }
           __syncwarp();
+        }
+        if (!ok) break;
+        // Reserve the next unit now that this unit's copies are all queued. Its Q load waits for q_free,
+        // which follows this unit's last Q.K^T a few tiles later, so the counter's round trip (~1000 cycles)
+        // no longer delays it (it did when the unit was taken after q_free). Reserving at the start of a
+        // unit instead weakened the longest-first balance (measured 0.5-8% slower). One wave (units <= CTAs):
+        // every unit was some CTA's first and the counter is not used.
+        if (n_units > (int)gridDim.x) {
+          int got = 0;
+          if (lane == 0) got = (int)gridDim.x + atomicAdd(work_ctr, 1);
+          next_u = __shfl_sync(0xffffffffu, got, 0);
+        } else {
+          next_u = n_units;
         }
       }
       // Drain: every issued copy must land before this CTA's shared memory can be released.
@@ -456,9 +491,8 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
         int qc[2] = {0, 0};          // S products per Q tile (separate S)
         bool ok = true;
         for (;;) {
-          const int u = next_unit(nu, ok);
-          if (u < 0) break;
-          const Unit x = unit_of(u);
+          const Unit x = next_unit(nu, ok);
+          if (x.id < 0) break;
           const int ng = x.has_b ? 2 : 1;
           const int total = C::SHARED_S ? ng * x.n_kv : x.n_kv;
           for (int k = 0; ok && k < total; ++k) {
@@ -496,9 +530,8 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
         int pc[2] = {0, 0}, uc[2] = {0, 0};  // P.V products and units per Q tile
         bool ok = true;
         for (;; ++nu) {
-          const int u = next_unit(nu, ok);
-          if (u < 0) break;
-          const Unit x = unit_of(u);
+          const Unit x = next_unit(nu, ok);
+          if (x.id < 0) break;
           const int ng = x.has_b ? 2 : 1;
           const uint32_t idesc_pv = idesc_f16(head_pv_bf16(x.bh), BM, D, true);
           auto issue_pv = [&](int g, int stage, bool acc) {
@@ -548,13 +581,12 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
     const uint32_t t_s = tmem + lane_off + (g ? C::T_S1 : C::T_S0);
     const uint32_t t_p = tmem + lane_off + (g ? C::T_P1 : C::T_P0);
     const uint32_t t_o = tmem + lane_off + (g ? C::T_O1 : C::T_O0);
-    const bool o_align32 = (reinterpret_cast<uintptr_t>(O) & 31) == 0;
+    const uint32_t o_stage = sbase + C::OFF_OST + (uint32_t)warp * C::OST_WARP;  // this warp's O staging block
     int sc = 0, oc = 0;  // S products read and P.V products waited for, this Q tile, all units
     bool ok = true;
     for (int nu = 0;; ++nu) {
-      const int u = next_unit(nu, ok);
-      if (u < 0) break;
-      Unit x = unit_of(u);
+      Unit x = next_unit(nu, ok);
+      if (x.id < 0) break;
       if (g == 1 && !x.has_b) continue;
       const bool pv_bf16 = head_pv_bf16(x.bh);
       const int n_kv = x.n_kv;
@@ -638,29 +670,37 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
       if (!ok) break;
       ++oc;
       tc_fence_after();
-      if constexpr (KV_PARTS) x = unit_of(u);  // derived again: fewer registers live across the tile loop
-      uint16_t* out = O + ((size_t)x.bh * N + row) * D;
+      x = read_unit(nu % kUnitRing);  // read again: fewer registers live across the tile loop
       if (!KV_PARTS || x.part < 0) {
+        // O / l through shared memory to a TMA store: each warp writes its 32 rows, 64 columns at a time, into
+        // its staging block in the output map's 128-byte swizzled layout (16-byte chunk k of a row at chunk
+        // k ^ (row % 8): conflict-free) and lane 0 stores the block; the store runs asynchronously, clipped at
+        // row N. Storing each thread's row straight to global memory (32 rows per warp instruction) took
+        // 1-3 K cycles per unit and held up the warp's next shared-memory accesses while the stores drained.
         const float inv_l = 1.f / l;
+        const int wrow0 = tile_row0 + (warp & 3) * 32;  // first row of this warp's 32-row slab
 #pragma unroll
-        for (int c = 0; c < D / 32; ++c) {
-          uint32_t rr[32];
-          tmem_ld32_wait(t_o + c * 32, rr);
-          uint32_t w[16];
+        for (int cb = 0; cb < D / 64; ++cb) {
+          if (lane == 0) bulk_wait_read_all();  // the previous store from this block has read it
+          __syncwarp();
 #pragma unroll
-          for (int i = 0; i < 16; ++i)
-            w[i] = pack2<BF16>(__uint_as_float(rr[2 * i]) * inv_l, __uint_as_float(rr[2 * i + 1]) * inv_l);
-          if (row < N) {
-            // 64 bytes of the row: two 32-byte stores (measured +0.2% to +3% over 16-byte ones) when O is
-            // 32-byte aligned (every row and chunk offset then is), else four 16-byte stores
-            if (o_align32) {
-              st_global_v8(out + c * 32, w);
-              st_global_v8(out + c * 32 + 16, w + 8);
-            } else {
-              uint4* dst = reinterpret_cast<uint4*>(out + c * 32);
+          for (int h = 0; h < 2; ++h) {
+            uint32_t rr[32];
+            tmem_ld32_wait(t_o + cb * 64 + h * 32, rr);
+            uint32_t w[16];
 #pragma unroll
-              for (int i = 0; i < 4; ++i) dst[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
-            }
+            for (int i = 0; i < 16; ++i)
+              w[i] = pack2<BF16>(__uint_as_float(rr[2 * i]) * inv_l, __uint_as_float(rr[2 * i + 1]) * inv_l);
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+              st_shared_v4(o_stage + lane * 128 + (uint32_t)(((4 * h + k) ^ (lane & 7)) * 16), w[4 * k], w[4 * k + 1],
+                           w[4 * k + 2], w[4 * k + 3]);
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0 && wrow0 < N) {
+            tma_store_3d(&tmO, o_stage, cb * 64, wrow0, x.bh);
+            bulk_commit();
           }
         }
       } else if constexpr (KV_PARTS) {
@@ -681,6 +721,7 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
       tc_fence_before();
       mbar_arrive(o_free(g));  // the next unit's first P.V may overwrite O now
     }
+    if (lane == 0) bulk_wait_all();  // this warp's O stores have completed (and read its staging block)
   }
 
   tc_fence_before();
@@ -996,6 +1037,9 @@ cudaError_t launch_t(const LaunchArgs& a, const Plan& p, const CUtensorMap& mq, 
   }
   if ((p.uses_counter && s.ctr == nullptr) || (p.tail_kv && (s.part_o == nullptr || s.part_ml == nullptr)))
     return cudaErrorInvalidValue;
+  // O is written by TMA stores of 32-row x 64-column blocks (one per softmax warp), clipped at row N
+  CUtensorMap mo;
+  if (!make_map(&mo, a.o, a.BH, a.N, D, BF16, 32)) return cudaErrorInvalidValue;
   const float scale_log2 = 1.4426950408889634f / sqrtf((float)D);
   tc::Tail tail{p.tail_from, p.tail_pieces, p.tail_kv ? 1 : 0, s.part_o, s.part_ml};
   timing_begin(a.stream);
@@ -1009,7 +1053,7 @@ cudaError_t launch_t(const LaunchArgs& a, const Plan& p, const CUtensorMap& mq, 
   attr_pdl[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr_pdl;
   cfg.numAttrs = 1;
-  cudaError_t el = cudaLaunchKernelEx(&cfg, kern, mq, mk, mv, mvh, (const int*)s.flags, static_cast<uint16_t*>(a.o),
+  cudaError_t el = cudaLaunchKernelEx(&cfg, kern, mq, mk, mv, mvh, mo, (const int*)s.flags, static_cast<uint16_t*>(a.o),
                                       a.BH, a.N, scale_log2, a.causal ? 1 : 0, p.group_heads, tail, a.status, s.ctr);
   if (el != cudaSuccess) return el;
   note_launch();
