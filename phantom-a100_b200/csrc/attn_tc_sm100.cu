@@ -136,13 +136,24 @@ __device__ __forceinline__ float row_max(const float (&s)[N]) {
 }
 
 // V staging for bf16 inputs: Vh = fp16(V), per (head, chunk) flag = 1 if a finite V value of the
-// chunk lies outside the fp16 range (it would become inf). Grid (kVChunks, BH), 16-byte vectors.
+// chunk lies outside the fp16 range (it would become inf). Grid (n_chunks, BH), 16-byte vectors; n_chunks =
+// v_chunks(BH), a multiple of 32, so that few heads still give every SM several blocks (with 32 chunks per
+// head a 4-head call ran 128 blocks: 14-16 us for 32 MiB, latency-bound). Block (0, 0) also zeroes the
+// attention kernel's work counter (`ctr`, may be null), which that kernel reads only after this one completes.
+// Launched with programmatic stream serialization: it waits for the previous work on the stream before
+// touching memory (its scratch may be memory the previous call on the stream released).
 constexpr int kVChunks = 32;
+__host__ __device__ constexpr int v_chunks(int BH) {
+  return 32 * (BH >= 20 ? 1 : ((640 + 32 * BH - 1) / (32 * BH) < 16 ? (640 + 32 * BH - 1) / (32 * BH) : 16));
+}
 
 __global__ void __launch_bounds__(256)
-stage_v_f16(const uint4* __restrict__ V, uint4* __restrict__ Vh, int* __restrict__ flags, long long vec_per_head) {
+stage_v_f16(const uint4* __restrict__ V, uint4* __restrict__ Vh, int* __restrict__ flags, long long vec_per_head,
+            int n_chunks, int* __restrict__ ctr) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const int bh = blockIdx.y;
-  const long long per_chunk = (vec_per_head + kVChunks - 1) / kVChunks;
+  if (ctr != nullptr && blockIdx.x == 0 && bh == 0 && threadIdx.x == 0) *ctr = 0;
+  const long long per_chunk = (vec_per_head + n_chunks - 1) / n_chunks;
   const long long b = (long long)blockIdx.x * per_chunk;
   const long long e = min(vec_per_head, b + per_chunk);
   const uint4* src = V + (long long)bh * vec_per_head;
@@ -160,7 +171,7 @@ stage_v_f16(const uint4* __restrict__ V, uint4* __restrict__ Vh, int* __restrict
     dst[i] = make_uint4(out[0], out[1], out[2], out[3]);
   }
   ovf = __syncthreads_or(ovf);
-  if (threadIdx.x == 0) flags[bh * kVChunks + blockIdx.x] = ovf;
+  if (threadIdx.x == 0) flags[bh * n_chunks + blockIdx.x] = ovf;
 }
 
 // p = exp2(s*scale - m_sub) for 64 scores of a row (s[OFF .. OFF+63]), packed as 16-bit pairs into p[32];
@@ -229,8 +240,8 @@ template <int D, bool BF16, bool KV_PARTS>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
 attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
             const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmVh,
-            const __grid_constant__ CUtensorMap tmO, const int* __restrict__ vflags, uint16_t* __restrict__ O,
-            int BH, int N, float scale_log2, int causal,
+            const __grid_constant__ CUtensorMap tmO, const int* __restrict__ vflags, int vchunks,
+            uint16_t* __restrict__ O, int BH, int N, float scale_log2, int causal,
             int group_heads, const Tail tail, int* __restrict__ status, int* __restrict__ work_ctr) {
   using C = Cfg<D>;
   constexpr int BN = C::BN;
@@ -307,11 +318,13 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
     }
     return x;
   };
-  // P.V precision of a head (warp-wide: one flag per lane): fp16 unless a V value of the head
-  // overflows fp16 (bf16 inputs).
+  // P.V precision of a head (warp-wide: each lane ORs vchunks / 32 chunk flags): fp16 unless a V value of the
+  // head overflows fp16 (bf16 inputs).
   auto head_pv_bf16 = [&](int bh) -> bool {
     if (!BF16) return false;
-    return __any_sync(0xffffffffu, vflags[bh * kVChunks + lane] != 0);
+    int f = 0;
+    for (int i = lane; i < vchunks; i += 32) f |= vflags[bh * vchunks + i];
+    return __any_sync(0xffffffffu, f != 0);
   };
 
   if (threadIdx.x == 0) {
@@ -426,7 +439,7 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
             mbar_arrive_expect_tx(kv_full(s), C::KV_TILE);
             for (int c = 0; c < C::KBLK; ++c)
               tma_load_3d(sbase + C::OFF_KV + s * C::KV_TILE + c * C::KV_SUB, m, kv_full(s), c * 64,
-                          (x.kv0 + (jt >> 1)) * BN, x.bh);
+                          ((KV_PARTS ? x.kv0 : 0) + (jt >> 1)) * BN, x.bh);
           }
           __syncwarp();
         }
@@ -610,7 +623,7 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
         ld_row<BN>(t_s, s);
         tc_fence_before();
         mbar_arrive(s_free(C::SHARED_S ? 0 : g));  // the next Q.K^T may overwrite S now
-        const int j0 = (x.kv0 + j) * BN;  // x.kv0 = 0 without K/V parts
+        const int j0 = ((KV_PARTS ? x.kv0 : 0) + j) * BN;  // first key of this K/V tile
         if (j0 + BN > N || (causal && j0 + BN - 1 > tile_row0)) {
           // columns c >= lim lie past N or (causal) after this row
           const int lim = min(N, causal ? row + 1 : N) - j0;
@@ -739,6 +752,7 @@ template <int D, bool BF16>
 __global__ void __launch_bounds__(BM)
 merge_kv_parts(const float4* __restrict__ part_o, const float2* __restrict__ part_ml, uint16_t* __restrict__ O,
                int BH, int N, int n_qblk, int group_heads, int tail_from, int P) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // launched as a programmatic dependent of the attention kernel
   const int tb = blockIdx.x, g = blockIdx.y, c = blockIdx.z, r = threadIdx.x;
   int bh, qt0;
   block_coords(tail_from + tb, BH, n_qblk, group_heads, &bh, &qt0);
@@ -1053,36 +1067,59 @@ cudaError_t launch_t(const LaunchArgs& a, const Plan& p, const CUtensorMap& mq, 
   attr_pdl[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr_pdl;
   cfg.numAttrs = 1;
-  cudaError_t el = cudaLaunchKernelEx(&cfg, kern, mq, mk, mv, mvh, mo, (const int*)s.flags, static_cast<uint16_t*>(a.o),
+  cudaError_t el = cudaLaunchKernelEx(&cfg, kern, mq, mk, mv, mvh, mo, (const int*)s.flags, tc::v_chunks(a.BH),
+                                      static_cast<uint16_t*>(a.o),
                                       a.BH, a.N, scale_log2, a.causal ? 1 : 0, p.group_heads, tail, a.status, s.ctr);
   if (el != cudaSuccess) return el;
   note_launch();
   cudaError_t e = cudaGetLastError();
   if (e == cudaSuccess && p.tail_kv) {
+    // programmatic dependent launch: the merge's blocks are scheduled as the attention CTAs exit and wait in
+    // the kernel (griddepcontrol.wait) for the whole attention grid, instead of for a launch after it
     const int n_qblk = ((a.N + tc::BM - 1) / tc::BM + 1) / 2;
-    tc::merge_kv_parts<D, BF16><<<dim3(p.n_tail, 2, D / 32), tc::BM, 0, a.stream>>>(
-        s.part_o, s.part_ml, static_cast<uint16_t*>(a.o), a.BH, a.N, n_qblk, p.group_heads, p.tail_from, p.tail_pieces);
-    note_launch();
-    e = cudaGetLastError();
+    cudaLaunchConfig_t mcfg = {};
+    mcfg.gridDim = dim3(p.n_tail, 2, D / 32);
+    mcfg.blockDim = dim3(tc::BM);
+    mcfg.stream = a.stream;
+    mcfg.attrs = attr_pdl;
+    mcfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&mcfg, tc::merge_kv_parts<D, BF16>, (const float4*)s.part_o, (const float2*)s.part_ml,
+                           static_cast<uint16_t*>(a.o), a.BH, a.N, n_qblk, p.group_heads, p.tail_from, p.tail_pieces);
+    if (e == cudaSuccess) {
+      note_launch();
+      e = cudaGetLastError();
+    }
   }
   timing_end(a.stream);
   return e;
 }
 
-// One call in the scratch `s`: zero the counters, stage V as fp16 (bf16), run the attention kernel.
+// One call in the scratch `s`: zero the work counter (fp16: a memset; bf16: the staging kernel does it), stage
+// V as fp16 (bf16), run the attention kernel.
 template <int D>
 cudaError_t run_d(const LaunchArgs& a, const Plan& p, const CUtensorMap& mq, const CUtensorMap& mk,
                   const CUtensorMap& mv, const Scratch& s, int dev) {
-  if (const size_t cb = counters_used(p)) {
+  const bool bf16 = a.dtype == PHANTOM_ATTN_BF16;
+  if (const size_t cb = counters_used(p); cb && !bf16) {
     cudaError_t e = cudaMemsetAsync(s.ctr, 0, cb, a.stream);
     if (e != cudaSuccess) return e;
   }
-  if (a.dtype != PHANTOM_ATTN_BF16) return launch_t<D, false>(a, p, mq, mk, mv, mv, s, dev);
+  if (!bf16) return launch_t<D, false>(a, p, mq, mk, mv, mv, s, dev);
   const long long vec_per_head = (long long)a.N * D / 8;
-  tc::stage_v_f16<<<dim3(tc::kVChunks, a.BH), 256, 0, a.stream>>>(
-      static_cast<const uint4*>(a.v), static_cast<uint4*>(s.vh), s.flags, vec_per_head);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(tc::v_chunks(a.BH), a.BH);
+  cfg.blockDim = dim3(256);
+  cfg.stream = a.stream;
+  cudaLaunchAttribute attr_pdl[1];
+  attr_pdl[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr_pdl[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr_pdl;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, tc::stage_v_f16, static_cast<const uint4*>(a.v), static_cast<uint4*>(s.vh),
+                                     s.flags, vec_per_head, tc::v_chunks(a.BH), counters_used(p) ? s.ctr : (int*)nullptr);
+  if (e != cudaSuccess) return e;
   note_launch();
-  cudaError_t e = cudaGetLastError();
+  e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   CUtensorMap mvh;
   if (!make_map(&mvh, s.vh, a.BH, a.N, D, false, tc::Cfg<D>::BN)) return cudaErrorInvalidValue;
@@ -1090,7 +1127,7 @@ cudaError_t run_d(const LaunchArgs& a, const Plan& p, const CUtensorMap& mq, con
 }
 
 size_t staged_v_bytes(int BH, int N, int d) { return (size_t)BH * N * d * 2; }
-size_t flag_bytes(int BH) { return (size_t)BH * tc::kVChunks * sizeof(int); }
+size_t flag_bytes(int BH) { return (size_t)BH * tc::v_chunks(BH) * sizeof(int); }
 
 // Allocating path: the launch's scratch [counters | K/V-part partials | fp16 V | flags] is one block from
 // the library's stream-ordered pool, taken and released on the caller's stream. Launches that overlap on
