@@ -89,10 +89,10 @@ struct Cfg {
   static constexpr int OFF_Q = 0;
   static constexpr int OFF_KV = 2 * Q_TILE;
   static constexpr int OFF_BAR = OFF_KV + STAGES * KV_TILE;
-  // barriers: q_full, kv_full[STAGES], kv_empty[STAGES], s_full[2], s_free[2], p_ready[2], o_done[2],
-  // drain (S issuer), drain (P.V issuer), q_free, o_free[2]
-  static constexpr int NUM_BARS = 1 + 2 * STAGES + 13;
-  static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;  // TMEM base address, abort flag, unit ring
+  // barriers: q_full[0], kv_full[STAGES], kv_empty[STAGES], s_full[2], s_free[2], p_ready[2], o_done[2],
+  // drain (S issuer), drain (P.V issuer), q_free, o_free[2], q_full[1]
+  static constexpr int NUM_BARS = 1 + 2 * STAGES + 14;
+  static constexpr int OFF_MISC = (OFF_BAR + NUM_BARS * 8 + 15) / 16 * 16;  // TMEM base address, abort flag, unit ring
   // O staging for the TMA-store epilogue: per softmax warp one 32-row x 64-column 16-bit block (4 KB) in the
   // 128-byte swizzled layout of the output tensor map (1024-byte aligned)
   static constexpr int OST_WARP = 32 * 128;
@@ -249,7 +249,11 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sbase = smem_u32(smem);
   const uint32_t bar0 = sbase + C::OFF_BAR;
-  auto q_full = [&]() { return bar0; };
+  // q_full[u & 1]: unit u is published and its Q tiles have landed. Two barriers used by alternate units: a
+  // consumer role may fall up to two units behind the producer (causal two-tile units of two K/V tiles, where
+  // tile A runs one, let B and the issuers finish the next unit while A still writes its output), and
+  // parity waits on a single barrier would then alias.
+  auto q_full = [&](int u) { return (u & 1) ? bar0 + 8u * (14 + 2 * C::STAGES) : bar0; };
   auto kv_full = [&](int s) { return bar0 + 8u * (1 + s); };
   auto kv_empty = [&](int s) { return bar0 + 8u * (1 + C::STAGES + s); };
   auto s_full = [&](int g) { return bar0 + 8u * (1 + 2 * C::STAGES + g); };
@@ -328,7 +332,8 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
   };
 
   if (threadIdx.x == 0) {
-    mbar_init(q_full(), 1);
+    mbar_init(q_full(0), 1);
+    mbar_init(q_full(1), 1);
     for (int s = 0; s < C::STAGES; ++s) {
       mbar_init(kv_full(s), 1);
       mbar_init(kv_empty(s), 1);
@@ -378,7 +383,7 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
   };
   // Next unit of a consumer role: wait for the unit's q_full phase, read the published unit (id -1: none).
   auto next_unit = [&](int nu, bool& ok) -> Unit {
-    ok = __all_sync(0xffffffffu, mbar_wait(q_full(), nu & 1, abort_flag, status, kErrMmaWait));
+    ok = __all_sync(0xffffffffu, mbar_wait(q_full(nu), (nu >> 1) & 1, abort_flag, status, kErrMmaWait));
     if (ok) return read_unit(nu % kUnitRing);
     Unit x;
     x.id = -1;
@@ -411,7 +416,7 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
             end.bh = end.row0 = end.kv0 = end.n_kv = end.part = end.tb = end.has_b = 0;
             end.id = -1;
             publish_unit(nu % kUnitRing, end);
-            mbar_arrive(q_full());  // release semantics: the consumers' wait sees the unit
+            mbar_arrive(q_full(nu));  // release semantics: the consumers' wait sees the unit
           }
           __syncwarp();
           ++nq_arrivals;
@@ -422,10 +427,11 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
         const int nq = x.has_b ? 2 : 1;
         if (elect_one()) {
           publish_unit(nu % kUnitRing, x);
-          mbar_arrive_expect_tx(q_full(), nq * C::Q_TILE);
+          mbar_arrive_expect_tx(q_full(nu), nq * C::Q_TILE);
           for (int g = 0; g < nq; ++g)
             for (int c = 0; c < C::KBLK; ++c)
-              tma_load_3d(sbase + C::OFF_Q + g * C::Q_TILE + c * C::Q_SUB, &tmQ, q_full(), c * 64, x.row0 + g * BM, x.bh);
+              tma_load_3d(sbase + C::OFF_Q + g * C::Q_TILE + c * C::Q_SUB, &tmQ, q_full(nu), c * 64, x.row0 + g * BM,
+                          x.bh);
         }
         __syncwarp();
         ++nu;
@@ -458,8 +464,9 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
         }
       }
       // Drain: every issued copy must land before this CTA's shared memory can be released.
-      // (phases complete in order: the last q_full phase started covers every Q copy)
-      if (nq_arrivals > 0) mbar_wait_drain(q_full(), (nq_arrivals - 1) & 1);
+      // (phases of a barrier complete in order: the last phase started on each q_full barrier covers its Q copies)
+      for (int a = nq_arrivals - 2; a < nq_arrivals; ++a)
+        if (a >= 0) mbar_wait_drain(q_full(a), (a >> 1) & 1);
       if (!ok) *abort_flag = 1;  // consumers waiting for a unit id stop at once
       for (int i = (t > C::STAGES ? t - C::STAGES : 0); i < t; ++i) mbar_wait_drain(kv_full(i % C::STAGES), (i / C::STAGES) & 1);
     }
@@ -495,11 +502,11 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
             mma_ss(d_t, dq + (a_off + oa), dk + (b_off + ob), idesc_qk, kk > 0 ? 1u : 0u);
           }
         };
-        // Shared S region (d = 128): one sequence of products over all units, in a unit Q tile k % ng
-        // against K tile k / ng; each product is issued once the softmax has read the previous one
-        // (s_free). One S region per Q tile (d = 64): per K tile, Q tile A then B, each once that tile's
-        // softmax has read its previous S. After a unit's last product, q_free lets the producer load
-        // the next unit's Q.
+        // Per K tile, Q tile A then B. Shared S region (d = 128): one sequence of products over all units,
+        // each issued once the softmax has read the previous one (s_free). One S region per Q tile
+        // (d = 64): each product issued once that tile's softmax has read its previous S. After a unit's
+        // last product, q_free lets the producer load the next unit's Q. Causal two-tile units: the last K
+        // tile (keys row0 + 128 ... row0 + 255) lies entirely after tile A's rows, so only B runs it.
         int tb = 0, nu = 0, ks = 0;  // first K/V copy of the unit, units done, S products (shared S)
         int qc[2] = {0, 0};          // S products per Q tile (separate S)
         bool ok = true;
@@ -507,13 +514,11 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
           const Unit x = next_unit(nu, ok);
           if (x.id < 0) break;
           const int ng = x.has_b ? 2 : 1;
-          const int total = C::SHARED_S ? ng * x.n_kv : x.n_kv;
-          for (int k = 0; ok && k < total; ++k) {
-            const int q = C::SHARED_S ? k / ng : k;
-            const int g0 = C::SHARED_S ? k % ng : 0;
+          const bool skip_a = causal && x.has_b;  // tile A skips the unit's last K tile
+          for (int q = 0; ok && q < x.n_kv; ++q) {
             const int tk = tb + 2 * q, sk = tk % C::STAGES;
-            if (g0 == 0 && !(ok = kv_wait(tk))) break;
-            for (int g = g0; g < (C::SHARED_S ? g0 + 1 : ng); ++g) {
+            if (!(ok = kv_wait(tk))) break;
+            for (int g = (skip_a && q == x.n_kv - 1) ? 1 : 0; g < ng; ++g) {
               const int n_prev = C::SHARED_S ? ks : qc[g];
               if (n_prev > 0 && !(ok = wait(s_free(C::SHARED_S ? 0 : g), (n_prev - 1) & 1))) break;
               tc_fence_after();
@@ -555,10 +560,11 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
             for (int kk = 0; kk < BN / 16; ++kk)
               mma_ts(d_t, p_t + kk * 8, dv + (b_off + kk * (2048 >> 4)), idesc_pv, (acc || kk > 0) ? 1u : 0u);
           };
+          const bool skip_a = causal && x.has_b;  // tile A skips the unit's last V tile (all its keys masked)
           for (int p = 0; ok && p < x.n_kv; ++p) {
             const int tv = tb + 2 * p + 1, sv = tv % C::STAGES;
             if (!(ok = kv_wait(tv))) break;
-            for (int g = 0; g < ng; ++g) {
+            for (int g = (skip_a && p == x.n_kv - 1) ? 1 : 0; g < ng; ++g) {
               if (p == 0 && uc[g] > 0 && !(ok = wait(o_free(g), (uc[g] - 1) & 1))) break;
               if (!(ok = wait(p_ready(g), pc[g] & 1))) break;
               tc_fence_after();
@@ -602,7 +608,8 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
       if (x.id < 0) break;
       if (g == 1 && !x.has_b) continue;
       const bool pv_bf16 = head_pv_bf16(x.bh);
-      const int n_kv = x.n_kv;
+      // causal two-tile unit: the last K/V tile lies entirely after tile A's rows, and A skips it
+      const int n_kv = x.n_kv - ((causal && x.has_b && g == 0) ? 1 : 0);
       const int tile_row0 = x.row0 + g * BM;
       const int row = tile_row0 + r_local;
       float m_used = -CUDART_INF_F, l = 0.f;

@@ -120,6 +120,19 @@ def test_persistent_ctas_mixed_units(capi, d, causal):
     assert_parity(np64(o), ref, "float16", f"160 heads d={d} causal={causal}")
 
 
+@pytest.mark.parametrize("d", [64, 128])
+@pytest.mark.parametrize("n", [129, 256])
+def test_causal_two_tile_units_back_to_back(capi, d, n):
+    """Causal, 400 heads of two Q tiles: every unit has two K/V tiles and tile A runs only the first (the
+    second lies after all of A's rows), so B and the issuers can finish a unit while A still writes the
+    previous one; several units per persistent CTA. Checks the results and that no bounded wait expired."""
+    q, k, v = make_qkv(4, 100, n, d, torch.bfloat16, seed=31 + n + d)
+    o = run_capi(capi, "fused_tc", q, k, v, True)
+    assert capi.device_status() == 0, "a bounded device wait expired"
+    ref = attention_naive(np64(q), np64(k), np64(v), True)
+    assert_parity(np64(o), ref, "bfloat16", f"400 heads N={n} d={d} causal")
+
+
 def test_bf16_fallback_heads_among_fp16_p_heads(capi):
     """Every seventh of 160 bf16 heads holds a V value beyond the fp16 range: persistent CTAs switch
     between fp16 P (fp16-staged V) and bf16 P (original V) from one unit to the next."""
