@@ -69,8 +69,9 @@ int phantom_attn_fused_tc(const void* q, const void* k, const void* v, void* o, 
  *
  * Same arguments, checks, kernel and results as phantom_attn_fused_tc. Instead of allocating, it uses
  * a file-scope 64 MiB device array that every GPU loading the library holds until the process exits:
- * a 256-byte status region (the status word, and the work counter of the kernel's persistent CTAs,
- * reset by every call), then, for bf16 inputs, the fp16 copy of V (2 * BH * N * head_dim bytes) and
+ * a 256-byte status region (the status word; the work counters of the kernel's persistent CTAs and a
+ * word marking fp16-overflowing heads, all reset by every call), then, for bf16 inputs, the fp16 copy of
+ * V (2 * BH * N * head_dim bytes) and
  * its overflow flags (128 bytes per head from BH = 20 on, up to 2 KiB per head below that, where V is
  * staged in more chunks per head). bf16 inputs needing more than 64 MiB in all (BH * N * head_dim
  * above about 33.5 million) are rejected with PHANTOM_ATTN_ERR_UNSUPPORTED; fp16 inputs need no

@@ -138,21 +138,25 @@ __device__ __forceinline__ float row_max(const float (&s)[N]) {
 // V staging for bf16 inputs: Vh = fp16(V), per (head, chunk) flag = 1 if a finite V value of the
 // chunk lies outside the fp16 range (it would become inf). Grid (n_chunks, BH), 16-byte vectors; n_chunks =
 // v_chunks(BH), a multiple of 32, so that few heads still give every SM several blocks (with 32 chunks per
-// head a 4-head call ran 128 blocks: 14-16 us for 32 MiB, latency-bound). Block (0, 0) also zeroes the
-// attention kernel's work counter (`ctr`, may be null), which that kernel reads only after this one completes.
+// head a 4-head call ran 128 blocks: 14-16 us for 32 MiB, latency-bound). Block (0, 0) also zeroes the two
+// attention launches' work counters ctr[0], ctr[1], which they read only after this kernel completes, and a
+// block that finds an overflow writes the call's generation `gen` into *any_ovf (the second launch runs only
+// if it finds it there; a stale or arbitrary value merely costs that launch a scan).
 // Launched with programmatic stream serialization: it waits for the previous work on the stream before
 // touching memory (its scratch may be memory the previous call on the stream released).
-constexpr int kVChunks = 32;
 __host__ __device__ constexpr int v_chunks(int BH) {
   return 32 * (BH >= 20 ? 1 : ((640 + 32 * BH - 1) / (32 * BH) < 16 ? (640 + 32 * BH - 1) / (32 * BH) : 16));
 }
 
 __global__ void __launch_bounds__(256)
 stage_v_f16(const uint4* __restrict__ V, uint4* __restrict__ Vh, int* __restrict__ flags, long long vec_per_head,
-            int n_chunks, int* __restrict__ ctr) {
+            int n_chunks, int* __restrict__ ctr, unsigned long long* __restrict__ any_ovf, unsigned long long gen) {
   asm volatile("griddepcontrol.wait;" ::: "memory");
   const int bh = blockIdx.y;
-  if (ctr != nullptr && blockIdx.x == 0 && bh == 0 && threadIdx.x == 0) *ctr = 0;
+  if (blockIdx.x == 0 && bh == 0 && threadIdx.x == 0) {
+    ctr[0] = 0;
+    ctr[1] = 0;
+  }
   const long long per_chunk = (vec_per_head + n_chunks - 1) / n_chunks;
   const long long b = (long long)blockIdx.x * per_chunk;
   const long long e = min(vec_per_head, b + per_chunk);
@@ -171,7 +175,10 @@ stage_v_f16(const uint4* __restrict__ V, uint4* __restrict__ Vh, int* __restrict
     dst[i] = make_uint4(out[0], out[1], out[2], out[3]);
   }
   ovf = __syncthreads_or(ovf);
-  if (threadIdx.x == 0) flags[bh * n_chunks + blockIdx.x] = ovf;
+  if (threadIdx.x == 0) {
+    flags[bh * n_chunks + blockIdx.x] = ovf;
+    if (ovf) *any_ovf = gen;
+  }
 }
 
 // p = exp2(s*scale - m_sub) for 64 scores of a row (s[OFF .. OFF+63]), packed as 16-bit pairs into p[32];
@@ -236,13 +243,26 @@ __device__ __forceinline__ void block_coords(int blk, int BH, int n_qblk, int gr
 
 // KV_PARTS: the launch's tail is cut into K/V parts (Tail::kv = 1). A separate instantiation, so that every
 // other launch runs a kernel without the parts' bookkeeping (measured: carrying it cost 2-5% per tile).
-template <int D, bool BF16, bool KV_PARTS>
+// OVF_HEADS (bf16 inputs): a bf16 call is two launches. The first (OVF_HEADS = false) computes P.V with fp16 P
+// and the fp16 copy of V and skips every head whose V overflows fp16; the second (OVF_HEADS = true, launched
+// after it) computes exactly those heads with bf16 P and the original V, and returns at once unless the
+// staging kernel wrote this call's generation into *any_ovf. One kernel holding both P paths took 6-7% more
+// cycles on every bf16 shape (ncu; the second exponential path costs code and registers in the hot loop).
+template <int D, bool BF16, bool KV_PARTS, bool OVF_HEADS>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
 attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
             const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmVh,
             const __grid_constant__ CUtensorMap tmO, const int* __restrict__ vflags, int vchunks,
+            const unsigned long long* __restrict__ any_ovf, unsigned long long gen,
             uint16_t* __restrict__ O, int BH, int N, float scale_log2, int causal,
             int group_heads, const Tail tail, int* __restrict__ status, int* __restrict__ work_ctr) {
+  static_assert(BF16 || !OVF_HEADS, "only bf16 inputs have fp16-overflow heads");
+  if constexpr (OVF_HEADS) {
+    // before anything else (no barrier, no TMEM yet): wait for the work before this launch, then leave unless
+    // some head of this call overflowed fp16 (the whole CTA takes the same branch)
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    if (*reinterpret_cast<const volatile unsigned long long*>(any_ovf) != gen) return;
+  }
   using C = Cfg<D>;
   constexpr int BN = C::BN;
   extern __shared__ uint8_t smem_raw[];
@@ -322,9 +342,9 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
     }
     return x;
   };
-  // P.V precision of a head (warp-wide: each lane ORs vchunks / 32 chunk flags): fp16 unless a V value of the
-  // head overflows fp16 (bf16 inputs).
-  auto head_pv_bf16 = [&](int bh) -> bool {
+  // Whether a V value of head bh overflows fp16 (bf16 inputs; warp-wide: each lane ORs vchunks / 32 chunk
+  // flags). Such heads belong to the OVF_HEADS launch, the others to the first one.
+  auto head_overflows = [&](int bh) -> bool {
     if (!BF16) return false;
     int f = 0;
     for (int i = lane; i < vchunks; i += 32) f |= vflags[bh * vchunks + i];
@@ -399,17 +419,30 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
       int t = 0, nu = 0, nq_arrivals = 0;  // K/V copies, units issued, q_full phases started (+ end marker)
       int next_u = blockIdx.x;             // the unit this CTA runs next
       bool ok = true;
+      auto take_unit = [&]() -> int {  // the next unit id from the work counter (one wave: none left)
+        if (n_units <= (int)gridDim.x) return n_units;  // every unit was some CTA's first; no counter
+        int got = 0;
+        if (lane == 0) got = (int)gridDim.x + atomicAdd(work_ctr, 1);
+        return __shfl_sync(0xffffffffu, got, 0);
+      };
+      // a unit of a head that the other launch of a bf16 call computes (OVF_HEADS)
+      auto other_launch = [&](int u) -> bool {
+        if constexpr (!BF16) return false;
+        else return head_overflows(unit_of(u).bh) != OVF_HEADS;
+      };
       if (elect_one()) {
         tma_prefetch_desc(&tmQ);
         tma_prefetch_desc(&tmK);
-        tma_prefetch_desc(BF16 ? &tmVh : &tmV);
+        tma_prefetch_desc((BF16 && !OVF_HEADS) ? &tmVh : &tmV);
         tma_prefetch_desc(&tmO);
       }
       __syncwarp();
       for (;;) {
         if (nu > 0 && !(ok = __all_sync(0xffffffffu, mbar_wait(q_free(), (nu - 1) & 1, abort_flag, status, kErrTmaWait))))
           break;
-        const int u = next_u < n_units ? next_u : -1;
+        int u = next_u;
+        while (u < n_units && other_launch(u)) u = take_unit();
+        if (u >= n_units) u = -1;
         if (u < 0) {
           if (elect_one()) {
             Unit end;
@@ -423,7 +456,7 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
           break;
         }
         const Unit x = unit_of(u);
-        const CUtensorMap* tm_v = (BF16 && !head_pv_bf16(x.bh)) ? &tmVh : &tmV;
+        const CUtensorMap* tm_v = (BF16 && !OVF_HEADS) ? &tmVh : &tmV;
         const int nq = x.has_b ? 2 : 1;
         if (elect_one()) {
           publish_unit(nu % kUnitRing, x);
@@ -455,13 +488,7 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
         // no longer delays it (it did when the unit was taken after q_free). Reserving at the start of a
         // unit instead weakened the longest-first balance (measured 0.5-8% slower). One wave (units <= CTAs):
         // every unit was some CTA's first and the counter is not used.
-        if (n_units > (int)gridDim.x) {
-          int got = 0;
-          if (lane == 0) got = (int)gridDim.x + atomicAdd(work_ctr, 1);
-          next_u = __shfl_sync(0xffffffffu, got, 0);
-        } else {
-          next_u = n_units;
-        }
+        next_u = take_unit();
       }
       // Drain: every issued copy must land before this CTA's shared memory can be released.
       // (phases of a barrier complete in order: the last phase started on each q_full barrier covers its Q copies)
@@ -518,7 +545,12 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
           for (int q = 0; ok && q < x.n_kv; ++q) {
             const int tk = tb + 2 * q, sk = tk % C::STAGES;
             if (!(ok = kv_wait(tk))) break;
-            for (int g = (skip_a && q == x.n_kv - 1) ? 1 : 0; g < ng; ++g) {
+            // Unrolled over the two Q tiles. As a loop over [first, ng) the fp16 d = 128 instantiation took 13% more
+            // cycles than the bf16 one (5.72 M against 5.06 M on B = 1, H = 32, N = 16384, ncu); unrolled, 4.73 M
+            // (bf16 1% fewer, d = 64 unchanged).
+#pragma unroll
+            for (int g = 0; g < 2; ++g) {
+              if (g >= ng || (g == 0 && skip_a && q == x.n_kv - 1)) continue;
               const int n_prev = C::SHARED_S ? ks : qc[g];
               if (n_prev > 0 && !(ok = wait(s_free(C::SHARED_S ? 0 : g), (n_prev - 1) & 1))) break;
               tc_fence_after();
@@ -551,7 +583,7 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
           const Unit x = next_unit(nu, ok);
           if (x.id < 0) break;
           const int ng = x.has_b ? 2 : 1;
-          const uint32_t idesc_pv = idesc_f16(head_pv_bf16(x.bh), BM, D, true);
+          constexpr uint32_t idesc_pv = idesc_f16(OVF_HEADS, BM, D, true);  // bf16 P and V only in that launch
           auto issue_pv = [&](int g, int stage, bool acc) {
             const uint32_t b_off = (uint32_t)(stage * C::KV_TILE) >> 4;
             const uint32_t d_t = tmem + (g ? C::T_O1 : C::T_O0);
@@ -564,6 +596,8 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
           for (int p = 0; ok && p < x.n_kv; ++p) {
             const int tv = tb + 2 * p + 1, sv = tv % C::STAGES;
             if (!(ok = kv_wait(tv))) break;
+            // (left as a loop: unrolled like the S products above, with pc[] and uc[] in registers, config 4 took
+            // 4.8% more cycles)
             for (int g = (skip_a && p == x.n_kv - 1) ? 1 : 0; g < ng; ++g) {
               if (p == 0 && uc[g] > 0 && !(ok = wait(o_free(g), (uc[g] - 1) & 1))) break;
               if (!(ok = wait(p_ready(g), pc[g] & 1))) break;
@@ -607,7 +641,6 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
       Unit x = next_unit(nu, ok);
       if (x.id < 0) break;
       if (g == 1 && !x.has_b) continue;
-      const bool pv_bf16 = head_pv_bf16(x.bh);
       // causal two-tile unit: the last K/V tile lies entirely after tile A's rows, and A skips it
       const int n_kv = x.n_kv - ((causal && x.has_b && g == 0) ? 1 : 0);
       const int tile_row0 = x.row0 + g * BM;
@@ -671,12 +704,12 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
         }
         const float m_sub = m_used == -CUDART_INF_F ? 0.f : m_used;
         uint32_t p[32];
-        float psum = pv_bf16 ? softmax64<true, 0>(s, scale_log2, m_sub, p) : softmax64<false, 0>(s, scale_log2, m_sub, p);
+        float psum = softmax64<OVF_HEADS, 0>(s, scale_log2, m_sub, p);
         tmem_st32(t_p, p);
         bool next_test = false;
         if constexpr (!C::SHARED_S) next_test = j + 1 < n_kv && mbar_test(s_full(g), sc & 1);
         if constexpr (BN == 128) {
-          psum += pv_bf16 ? softmax64<true, 64>(s, scale_log2, m_sub, p) : softmax64<false, 64>(s, scale_log2, m_sub, p);
+          psum += softmax64<OVF_HEADS, 64>(s, scale_log2, m_sub, p);
           tmem_st32(t_p + 32, p);
         }
         tmem_wait_st();
@@ -754,15 +787,22 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
 
 // Merge of the K/V parts of a launch's tail blocks. Block (tail block, Q tile, 32-column chunk); thread =
 // query row. m = max_p m_p, O = sum_p 2^(m_p - m) O_p / sum_p 2^(m_p - m) l_p, summed over the parts in
-// their fixed order (results do not depend on which part ran first or where).
+// their fixed order (results do not depend on which part ran first or where). bf16 inputs: blocks of heads
+// whose V overflows fp16 were not cut into parts (the second launch computes them whole) and are skipped.
 template <int D, bool BF16>
 __global__ void __launch_bounds__(BM)
 merge_kv_parts(const float4* __restrict__ part_o, const float2* __restrict__ part_ml, uint16_t* __restrict__ O,
-               int BH, int N, int n_qblk, int group_heads, int tail_from, int P) {
+               int BH, int N, int n_qblk, int group_heads, int tail_from, int P, const int* __restrict__ vflags,
+               int vchunks) {
   asm volatile("griddepcontrol.wait;" ::: "memory");  // launched as a programmatic dependent of the attention kernel
   const int tb = blockIdx.x, g = blockIdx.y, c = blockIdx.z, r = threadIdx.x;
   int bh, qt0;
   block_coords(tail_from + tb, BH, n_qblk, group_heads, &bh, &qt0);
+  if constexpr (BF16) {
+    int f = 0;
+    for (int i = r; i < vchunks; i += BM) f |= vflags[bh * vchunks + i];
+    if (__syncthreads_or(f)) return;  // whole block: the head belongs to the second launch
+  }
   const int row = (qt0 + g) * BM + r;
   if (qt0 + g >= (N + BM - 1) / BM || row >= N) return;  // no second Q tile / past the end
   const size_t slot0 = ((size_t)tb * 2 + g) * P;
@@ -1016,23 +1056,33 @@ cudaError_t make_plan(const LaunchArgs& a, int dev, bool allow_kv_parts, Plan* p
   return cudaSuccess;
 }
 
-// Device memory one launch works in besides its inputs and output. `ctr`: the persistent CTAs' work
-// counter followed by the K/V-part counters (n_tail * 2 * 128 ints; both zeroed on the launch's stream
-// before the kernel runs). `part_o`, `part_ml`: the K/V parts' partial results. `vh`, `flags` (bf16 inputs
-// only): the fp16 copy of V and its per-(head, chunk) fp16-overflow flags.
+// Device memory one call works in besides its inputs and output. `ctr`: ctr[0] the persistent CTAs' work
+// counter; bf16 inputs also ctr[1], the work counter of the launch for fp16-overflow heads, and at ctr + 2 a
+// 64-bit word the staging kernel sets to the call's generation `gen` when some head overflows (16 bytes in all;
+// the counters are zeroed on the call's stream before the attention kernels run). `part_o`, `part_ml`: the K/V
+// parts' partial results. `vh`, `flags` (bf16 inputs only): the fp16 copy of V and its per-(head, chunk)
+// fp16-overflow flags.
 struct Scratch {
   int* ctr = nullptr;
   float4* part_o = nullptr;
   float2* part_ml = nullptr;
   void* vh = nullptr;
   int* flags = nullptr;
+  unsigned long long gen = 0;
 };
+
+// A value unique to each bf16 call in this process (never 0): what the staging kernel writes into the call's
+// overflow word, so the word needs no zeroing (a leftover value of another call can only differ).
+unsigned long long next_generation() {
+  static std::atomic<unsigned long long> count{0};
+  return 0x9E3779B97F4A7C15ull * (count.fetch_add(1, std::memory_order_relaxed) + 1);
+}
 
 size_t round256(size_t b) { return (b + 255) & ~size_t(255); }
 // Bytes of the work counter (zeroed before each launch) and of the K/V parts' partial results of a plan, 0
 // when unused; counter_bytes() is the 256-byte-aligned room the counter takes in an allocation.
-size_t counters_used(const Plan& p) { return p.uses_counter ? sizeof(int) : 0; }
-size_t counter_bytes(const Plan& p) { return round256(counters_used(p)); }
+size_t counters_used(const Plan& p, bool bf16) { return bf16 ? 16 : (p.uses_counter ? sizeof(int) : 0); }
+size_t counter_bytes(const Plan& p, bool bf16) { return round256(counters_used(p, bf16)); }
 size_t part_o_bytes(const Plan& p, int d) {
   return p.tail_kv ? (size_t)p.n_tail * 2 * p.tail_pieces * tc::BM * d * sizeof(float) : 0;
 }
@@ -1043,21 +1093,24 @@ size_t part_ml_bytes(const Plan& p) {
 template <int D, bool BF16>
 cudaError_t launch_t(const LaunchArgs& a, const Plan& p, const CUtensorMap& mq, const CUtensorMap& mk,
                      const CUtensorMap& mv, const CUtensorMap& mvh, const Scratch& s, int dev) {
-  auto kern = p.tail_kv ? tc::attn_fwd_tc<D, BF16, true> : tc::attn_fwd_tc<D, BF16, false>;
+  auto kern = p.tail_kv ? tc::attn_fwd_tc<D, BF16, true, false> : tc::attn_fwd_tc<D, BF16, false, false>;
   constexpr int smem = tc::Cfg<D>::SMEM_BYTES;
   std::atomic<bool>& attr = g_attr_set[D == 128 ? 1 : 0][dev];
   if (!attr.load(std::memory_order_acquire)) {
     // Every instantiation of one head dimension has the same shared-memory size; setting it twice is
     // harmless, so two threads racing here need no lock.
     cudaError_t e = cudaSuccess;
-    for (auto f : {tc::attn_fwd_tc<D, false, false>, tc::attn_fwd_tc<D, true, false>, tc::attn_fwd_tc<D, false, true>,
-                   tc::attn_fwd_tc<D, true, true>})
+    for (auto f : {tc::attn_fwd_tc<D, false, false, false>, tc::attn_fwd_tc<D, true, false, false>,
+                   tc::attn_fwd_tc<D, false, true, false>, tc::attn_fwd_tc<D, true, true, false>,
+                   tc::attn_fwd_tc<D, true, false, true>})
       if (e == cudaSuccess) e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     attr.store(true, std::memory_order_release);
   }
-  if ((p.uses_counter && s.ctr == nullptr) || (p.tail_kv && (s.part_o == nullptr || s.part_ml == nullptr)))
+  if (((p.uses_counter || BF16) && s.ctr == nullptr) || (p.tail_kv && (s.part_o == nullptr || s.part_ml == nullptr)))
     return cudaErrorInvalidValue;
+  const unsigned long long* any_ovf = BF16 ? reinterpret_cast<const unsigned long long*>(s.ctr + 2) : nullptr;
+  const int vchunks = tc::v_chunks(a.BH);
   // O is written by TMA stores of 32-row x 64-column blocks (one per softmax warp), clipped at row N
   CUtensorMap mo;
   if (!make_map(&mo, a.o, a.BH, a.N, D, BF16, 32)) return cudaErrorInvalidValue;
@@ -1074,9 +1127,9 @@ cudaError_t launch_t(const LaunchArgs& a, const Plan& p, const CUtensorMap& mq, 
   attr_pdl[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr_pdl;
   cfg.numAttrs = 1;
-  cudaError_t el = cudaLaunchKernelEx(&cfg, kern, mq, mk, mv, mvh, mo, (const int*)s.flags, tc::v_chunks(a.BH),
-                                      static_cast<uint16_t*>(a.o),
-                                      a.BH, a.N, scale_log2, a.causal ? 1 : 0, p.group_heads, tail, a.status, s.ctr);
+  cudaError_t el = cudaLaunchKernelEx(&cfg, kern, mq, mk, mv, mvh, mo, (const int*)s.flags, vchunks, any_ovf, s.gen,
+                                      static_cast<uint16_t*>(a.o), a.BH, a.N, scale_log2, a.causal ? 1 : 0,
+                                      p.group_heads, tail, a.status, s.ctr);
   if (el != cudaSuccess) return el;
   note_launch();
   cudaError_t e = cudaGetLastError();
@@ -1091,10 +1144,27 @@ cudaError_t launch_t(const LaunchArgs& a, const Plan& p, const CUtensorMap& mq, 
     mcfg.attrs = attr_pdl;
     mcfg.numAttrs = 1;
     e = cudaLaunchKernelEx(&mcfg, tc::merge_kv_parts<D, BF16>, (const float4*)s.part_o, (const float2*)s.part_ml,
-                           static_cast<uint16_t*>(a.o), a.BH, a.N, n_qblk, p.group_heads, p.tail_from, p.tail_pieces);
+                           static_cast<uint16_t*>(a.o), a.BH, a.N, n_qblk, p.group_heads, p.tail_from, p.tail_pieces,
+                           (const int*)s.flags, vchunks);
     if (e == cudaSuccess) {
       note_launch();
       e = cudaGetLastError();
+    }
+  }
+  if constexpr (BF16) {
+    // The launch for heads whose V overflows fp16: every query block whole (no tail split), its own work counter;
+    // it returns at once when the staging kernel found no overflow in this call.
+    if (e == cudaSuccess) {
+      const long long n_blk = (long long)(((a.N + tc::BM - 1) / tc::BM + 1) / 2) * a.BH;
+      tc::Tail whole{(int)n_blk, 1, 0, nullptr, nullptr};
+      cudaLaunchConfig_t ocfg = cfg;  // same persistent grid, block, shared memory, stream, programmatic launch
+      e = cudaLaunchKernelEx(&ocfg, tc::attn_fwd_tc<D, true, false, true>, mq, mk, mv, mvh, mo, (const int*)s.flags,
+                             vchunks, any_ovf, s.gen, static_cast<uint16_t*>(a.o), a.BH, a.N, scale_log2,
+                             a.causal ? 1 : 0, p.group_heads, whole, a.status, s.ctr + 1);
+      if (e == cudaSuccess) {
+        note_launch();
+        e = cudaGetLastError();
+      }
     }
   }
   timing_end(a.stream);
@@ -1107,7 +1177,7 @@ template <int D>
 cudaError_t run_d(const LaunchArgs& a, const Plan& p, const CUtensorMap& mq, const CUtensorMap& mk,
                   const CUtensorMap& mv, const Scratch& s, int dev) {
   const bool bf16 = a.dtype == PHANTOM_ATTN_BF16;
-  if (const size_t cb = counters_used(p); cb && !bf16) {
+  if (const size_t cb = counters_used(p, bf16); cb && !bf16) {
     cudaError_t e = cudaMemsetAsync(s.ctr, 0, cb, a.stream);
     if (e != cudaSuccess) return e;
   }
@@ -1123,7 +1193,8 @@ cudaError_t run_d(const LaunchArgs& a, const Plan& p, const CUtensorMap& mq, con
   cfg.attrs = attr_pdl;
   cfg.numAttrs = 1;
   cudaError_t e = cudaLaunchKernelEx(&cfg, tc::stage_v_f16, static_cast<const uint4*>(a.v), static_cast<uint4*>(s.vh),
-                                     s.flags, vec_per_head, tc::v_chunks(a.BH), counters_used(p) ? s.ctr : (int*)nullptr);
+                                     s.flags, vec_per_head, tc::v_chunks(a.BH), s.ctr,
+                                     reinterpret_cast<unsigned long long*>(s.ctr + 2), s.gen);
   if (e != cudaSuccess) return e;
   note_launch();
   e = cudaGetLastError();
@@ -1146,7 +1217,7 @@ cudaError_t launch_alloc(const LaunchArgs& a, const CUtensorMap& mq, const CUten
   cudaError_t e = make_plan<D>(a, dev, true, &p);
   if (e != cudaSuccess) return e;
   const bool bf16 = a.dtype == PHANTOM_ATTN_BF16;
-  const size_t cb = counter_bytes(p), ob = part_o_bytes(p, D), mb = part_ml_bytes(p);
+  const size_t cb = counter_bytes(p, bf16), ob = part_o_bytes(p, D), mb = part_ml_bytes(p);
   const size_t need = cb + ob + mb + (bf16 ? staged_v_bytes(a.BH, a.N, D) + flag_bytes(a.BH) : 0);
   if (need == 0) return run_d<D>(a, p, mq, mk, mv, Scratch{}, dev);
   cudaMemPool_t pool;
@@ -1156,6 +1227,7 @@ cudaError_t launch_alloc(const LaunchArgs& a, const CUtensorMap& mq, const CUten
   char* base = static_cast<char*>(block);
   Scratch s;
   if (cb) s.ctr = reinterpret_cast<int*>(base);
+  if (bf16) s.gen = next_generation();
   if (ob) {
     s.part_o = reinterpret_cast<float4*>(base + cb);
     s.part_ml = reinterpret_cast<float2*>(base + cb + ob);
@@ -1169,8 +1241,9 @@ cudaError_t launch_alloc(const LaunchArgs& a, const CUtensorMap& mq, const CUten
   return e != cudaSuccess ? e : ef;
 }
 
-// Caller-supplied scratch (no allocation): the work counter at `ctr`, [fp16 V | flags] at `scratch`. The
-// tail is never cut into K/V parts here (their partial results would need more scratch).
+// Caller-supplied scratch (no allocation): the counters (and, for bf16, the overflow word; 16 bytes) at `ctr`,
+// [fp16 V | flags] at `scratch`. The tail is never cut into K/V parts here (their partial results would need
+// more scratch).
 template <int D>
 cudaError_t launch_given(const LaunchArgs& a, const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
                          int dev, int* ctr, void* scratch) {
@@ -1179,6 +1252,7 @@ cudaError_t launch_given(const LaunchArgs& a, const CUtensorMap& mq, const CUten
   if (e != cudaSuccess) return e;
   Scratch s;
   s.ctr = ctr;
+  if (a.dtype == PHANTOM_ATTN_BF16) s.gen = next_generation();
   if (a.dtype == PHANTOM_ATTN_BF16) {
     s.vh = scratch;
     s.flags = reinterpret_cast<int*>(static_cast<char*>(scratch) + staged_v_bytes(a.BH, a.N, D));

@@ -162,10 +162,11 @@ int simt_entry(const char* name, const void* q, const void* k, const void* v, vo
 }
 
 // ------------------------------------------------------------------ entry point without allocation
-// Scratch of phantom_attn_fused_tc_noalloc, laid out as [status region (256 B: status word; the
-// persistent CTAs' work counter at byte 128) | fp16 copy of V | V overflow flags]. A file-scope device
-// array: every GPU that loads this library holds these 64 MiB until the process exits. All calls on a
-// device share it, the work counter included (each call zeroes it on its stream before its kernel).
+// Scratch of phantom_attn_fused_tc_noalloc, laid out as [status region (256 B: status word; at byte 128 the
+// persistent CTAs' work counters and the call's fp16-overflow word, 16 bytes) | fp16 copy of V | V overflow
+// flags]. A file-scope device array: every GPU that loads this library holds these 64 MiB until the process
+// exits. All calls on a device share it, the counters included (each call resets them on its stream before
+// its attention kernels run).
 constexpr size_t kNoAllocScratchBytes = size_t(64) << 20;
 constexpr size_t kNoAllocStatusBytes = 256;
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];

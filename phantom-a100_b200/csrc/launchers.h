@@ -22,9 +22,10 @@ struct LaunchArgs {
 cudaError_t launch_fused_tc_sm100(const LaunchArgs& a);
 // Dynamic shared memory the tensor-core kernel needs for head dim d.
 size_t fused_tc_smem_bytes(int d);
-// Tensor-core kernel with caller-supplied scratch (no allocation inside): `work_ctr` is the persistent
-// CTAs' work counter (one int, zeroed by the launch on its stream; calls that overlap on the GPU must not
-// share it), `scratch` the bf16 V staging buffer of fused_tc_scratch_bytes() bytes (0 for fp16 inputs).
+// Tensor-core kernel with caller-supplied scratch (no allocation inside): `work_ctr` is 16 bytes, 8-byte
+// aligned: the persistent CTAs' work counters (two ints, zeroed on the call's stream) and, for bf16 inputs, the
+// call's fp16-overflow word; calls that overlap on the GPU must not share it. `scratch` is the bf16 V staging
+// buffer of fused_tc_scratch_bytes() bytes (0 for fp16 inputs).
 cudaError_t launch_fused_tc_sm100_scratch(const LaunchArgs& a, int* work_ctr, void* scratch);
 size_t fused_tc_scratch_bytes(int BH, int N, int d, int dtype);
 
