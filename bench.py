@@ -142,10 +142,27 @@ class ClockSampler:
             self.proc = subprocess.Popen(cmd, stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         except OSError:
             self.proc = None
+            return
+        # nvidia-smi takes a while to start (longer with several ranks starting it at once); a timed region of
+        # a few milliseconds (8 GPUs sharing config 4) would otherwise end before its first sample
+        t0 = time.time()
+        while time.time() - t0 < 5.0 and self._lines() < 1 and self.proc.poll() is None:
+            time.sleep(0.01)
+
+    def _lines(self) -> int:
+        try:
+            with open(self.path) as f:
+                return sum(1 for line in f if line.count(",") >= 8)
+        except OSError:
+            return 0
 
     def stop(self) -> dict | None:
         if self.proc is None:
             return None
+        # at least one sample after the timed region (samples every 20 ms)
+        n, t0 = self._lines(), time.time()
+        while time.time() - t0 < 0.5 and self._lines() <= n and self.proc.poll() is None:
+            time.sleep(0.005)
         self.proc.terminate()
         try:
             self.proc.wait(timeout=5)
