@@ -9,7 +9,8 @@
 // bf16 inputs: Q K^T runs in bf16; V is first staged as fp16 by stage_v_f16 (exact for every bf16
 // value inside the fp16 range) so that P.V also runs with fp16 P - rounding P to bf16 instead would
 // alone give a relative-L2 error of ~2.4e-3, above the 1e-3 parity bound. A head whose V holds a
-// finite value beyond the fp16 range falls back to bf16 P and the original bf16 V for that head.
+// finite value beyond the fp16 range falls back to bf16 P and the original bf16 V for that head; the
+// call's main launch skips such heads and a second launch (OVF_HEADS) computes them.
 //
 // B200 mapping (not a translation of the WMMA kernel):
 //   * Work unit: two 128-row Q tiles (A, B) of one (batch, head), streaming K/V tiles of 128 keys.
@@ -36,6 +37,8 @@
 //     its own P.V product (only for the previous one, before it overwrites P and rescales O).
 //   * TMEM (512 columns): d = 128: S [0,128) used by tiles A and B in turn, P_A [128,192),
 //     P_B [192,256), O_A [256,384), O_B [384,512); d = 64: O_A, O_B, then S_A, S_B, P_A, P_B.
+//   * O leaves through shared memory: each softmax warp writes its 32 rows into a swizzled staging block
+//     and one lane issues a TMA store.
 //   * Every mbarrier wait is bounded; on expiry the CTA drains its in-flight copies and MMAs,
 //     frees TMEM, records the failure in the device status word and exits.
 #include <cuda.h>
