@@ -134,8 +134,9 @@ def test_causal_two_tile_units_back_to_back(capi, d, n):
 
 
 def test_bf16_fallback_heads_among_fp16_p_heads(capi):
-    """Every seventh of 160 bf16 heads holds a V value beyond the fp16 range: persistent CTAs switch
-    between fp16 P (fp16-staged V) and bf16 P (original V) from one unit to the next."""
+    """Every seventh of 160 bf16 heads holds a V value beyond the fp16 range: the call's main launch
+    (fp16 P, fp16-staged V) skips those heads and its second launch computes them with bf16 P and the
+    original V; every head must come out right."""
     q, k, v = make_qkv(1, 160, 300, 128, torch.bfloat16, seed=21)
     bad = list(range(0, 160, 7))
     for h in bad:
@@ -148,6 +149,32 @@ def test_bf16_fallback_heads_among_fp16_p_heads(capi):
     for h in bad:
         rel = np.linalg.norm(np64(o)[:, h] - ref[:, h]) / np.linalg.norm(ref[:, h])
         assert rel < 5e-3, (h, rel)
+
+
+@pytest.mark.parametrize("causal", [False, True])
+def test_overflow_heads_across_consecutive_calls(capi, causal):
+    """bf16 calls that alternate between V with and without fp16-overflowing heads (300 heads at N = 300,
+    several units per persistent CTA). A call's second launch must compute exactly its own overflowing
+    heads: one without any, made after one with them (its scratch may be the same memory), must leave every
+    head to the main launch, and one with them after one without must compute them."""
+    q, k, v = make_qkv(1, 300, 300, 128, torch.bfloat16, seed=23)
+    bad = list(range(3, 300, 37))
+    v_bad = v.clone()
+    for h in bad:
+        v_bad[0, h, (h * 7) % 300, h % 128] = 2.0e5  # beyond fp16's 65504, exact in bf16
+    ref_clean = attention_naive(np64(q), np64(k), np64(v), causal)
+    ref_bad = attention_naive(np64(q), np64(k), np64(v_bad), causal)
+    good = [h for h in range(300) if h not in bad]
+    for call, with_bad in enumerate([True, False, True, False]):
+        o = run_capi(capi, "fused_tc", q, k, v_bad if with_bad else v, causal)
+        ref = ref_bad if with_bad else ref_clean
+        assert_parity(np64(o)[:, good], ref[:, good], "bfloat16", f"call {call}: heads without overflow")
+        if with_bad:
+            for h in bad:
+                rel = np.linalg.norm(np64(o)[:, h] - ref[:, h]) / np.linalg.norm(ref[:, h])
+                assert rel < 5e-3, (call, h, rel)
+        else:
+            assert_parity(np64(o)[:, bad], ref[:, bad], "bfloat16", f"call {call}: formerly overflowing heads")
 
 
 @pytest.mark.parametrize("d", [64, 128])

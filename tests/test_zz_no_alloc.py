@@ -44,6 +44,24 @@ def test_noalloc_rejects_bf16_inputs_beyond_its_scratch(cuda_ok, capi):
     assert e.value.code == ERR_UNSUPPORTED and "scratch" in str(e.value)
 
 
+def test_noalloc_overflow_heads_across_consecutive_calls(cuda_ok, capi):
+    """bf16 calls through the allocation-free entry point share one static array, counters and overflow
+    word included: a call with fp16-overflowing V heads, one without, and one with again must each equal
+    the allocating entry point's result."""
+    q, k, v = make_qkv(1, 64, 600, 128, torch.bfloat16, seed=61)
+    v_bad = v.clone()
+    for h in range(5, 64, 11):
+        v_bad[0, h, (h * 13) % 600, h % 128] = 3.0e5  # beyond fp16's 65504
+    for call, vv in enumerate([v_bad, v, v_bad]):
+        o_ref = torch.empty_like(q)
+        capi.fused_tc(q, k, vv, o_ref)
+        o = torch.full_like(q, float("nan"))
+        capi.fused_tc_noalloc(q, k, vv, o)
+        torch.cuda.synchronize()
+        assert torch.equal(o, o_ref), f"noalloc call {call + 1} differs from fused_tc"
+    assert capi.device_status() == 0
+
+
 STATUS_PROBE, STATUS_NOALLOC = 16, 256  # include/phantom_attn.h
 
 
