@@ -25,9 +25,9 @@ How it works, in three steps that can run on different machines:
   3. read     the report with Nsight Compute's own Python reader (ncu_report, shipped with ncu under
               extras/python), in ncu's base units: time in ns, bytes, percent.
 
-A call of the bf16 path is two launches (stage_v_f16, then attn_fwd_tc), and a call whose last wave runs
-as K/V parts adds merge_kv_parts: `calls()` groups the launches of each call, and `aggregate()` combines
-them.
+A call of the bf16 path is three launches (stage_v_f16, the main attn_fwd_tc, and an attn_fwd_tc for heads
+whose V overflows fp16, which returns at once when there are none), and a call whose last wave runs as K/V
+parts adds merge_kv_parts: `calls()` groups the launches of each call, and `aggregate()` combines them.
 
     python -m cuda_attn.hw_counters --flops 4.398e12 --bytes 536870912 --out profiles/x.md -- \
         python bench.py --config config4 --steps 1 --warmup 1 --no-cpu-baseline
@@ -38,6 +38,7 @@ import argparse
 import glob
 import json
 import os
+import re
 import shlex
 import shutil
 import subprocess
@@ -152,13 +153,24 @@ def read_report(path: str, metrics: list[str], reader=None) -> list[dict]:
 MERGE_KERNEL = "merge_kv_parts"
 
 
+def is_overflow_launch(name: str) -> bool:
+    """Whether a launch is the second attention launch of a bf16 call, the one for heads whose V overflows
+    fp16: `attn_fwd_tc<D, BF16, KV_PARTS, OVF_HEADS>` with OVF_HEADS set."""
+    m = re.search(ATTENTION_KERNEL + r"<([^>]*)>", name)
+    if not m:
+        return False
+    args = [a.strip() for a in m.group(1).split(",")]
+    return len(args) >= 4 and args[3] in ("1", "true")
+
+
 def calls(launches: list[dict], last: str = ATTENTION_KERNEL) -> list[list[dict]]:
-    """Group launches into forward calls: each group ends with a launch of the attention kernel (a bf16
-    call is stage_v_f16 then attn_fwd_tc), plus the merge_kv_parts launch that follows it when the call
-    cut its last wave into K/V parts. Launches after the last attention kernel form no call."""
+    """Group launches into forward calls: each group ends with the main launch of the attention kernel (a
+    bf16 call is stage_v_f16 then attn_fwd_tc), followed by the merge_kv_parts launch when the call cut its
+    last wave into K/V parts and, for bf16, the attention launch for fp16-overflow heads. Launches after the
+    last main attention launch form no call."""
     groups, cur = [], []
     for rec in launches:
-        if MERGE_KERNEL in rec["kernel"] and groups and not cur:
+        if (MERGE_KERNEL in rec["kernel"] or is_overflow_launch(rec["kernel"])) and groups and not cur:
             groups[-1].append(rec)
             continue
         cur.append(rec)

@@ -97,6 +97,16 @@ def test_calls_group_staging_with_the_attention_kernel():
     assert [[r[T] for r in g] for g in groups] == [[1, 2], [3]]
 
 
+def test_calls_attach_the_overflow_heads_launch():
+    # a bf16 call: staging, main launch, K/V-part merge, the launch for fp16-overflow heads; then an fp16 call
+    ls = [launch("stage_v_f16", 1), launch("void attn_fwd_tc<128, 1, 1, 0>(...)", 2),
+          launch("void merge_kv_parts<128, 1>(...)", 3), launch("void attn_fwd_tc<128, 1, 0, 1>(...)", 4),
+          launch("void attn_fwd_tc<64, 0, 0, 0>(...)", 5)]
+    assert [[r[T] for r in g] for g in hc.calls(ls)] == [[1, 2, 3, 4], [5]]
+    assert hc.is_overflow_launch("attn_fwd_tc<128, true, false, true>")
+    assert not hc.is_overflow_launch("attn_fwd_tc<128, true, false, false>") and not hc.is_overflow_launch("stage_v_f16")
+
+
 def test_calls_attach_the_merge_of_k_v_parts():
     ls = [launch("tc::stage_v_f16", 1), launch("tc::attn_fwd_tc<128, true, true>", 2),
           launch("tc::merge_kv_parts<128, true>", 3), launch("tc::attn_fwd_tc<128, false, false>", 4)]
