@@ -1,0 +1,15 @@
+"""Entry point at the reference's path for the tile / launch-shape sweep (reference bench/sweep_tiles.py).
+
+    python bench/sweep_tiles.py [options]        # run from phantom-a100_b200/, as the reference runs it from its root
+
+The implementation is cuda_attn.sweep_tiles (same options as `python -m cuda_attn.sweep_tiles`).
+"""
+import os
+import sys
+
+sys.path.insert(0, os.path.join(os.path.dirname(os.path.abspath(__file__)), ".."))
+
+from cuda_attn.sweep_tiles import main  # noqa: E402
+
+if __name__ == "__main__":
+    sys.exit(main())

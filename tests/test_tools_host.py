@@ -191,3 +191,17 @@ def test_read_nsight_compute_sample_report():
         pytest.skip("no ncu_report module or sample report in this image")
     recs = hc.read_report(samples[0], [T, DR], reader)
     assert recs and recs[0][T] > 0 and recs[0][DR] > 0
+
+
+def test_tools_at_the_reference_paths():
+    """The reference runs its tools as `python bench/benchmark.py`, `bench/sweep_tiles.py`, `bench/run_one.py`
+    from its root and imports `autotune.hw_counters`; the same paths under phantom-a100_b200/ reach this
+    library's implementations."""
+    import sys
+    pkg = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "phantom-a100_b200")
+    for script, word in (("bench/benchmark.py", "--impls"), ("bench/sweep_tiles.py", "--dim"),
+                         ("bench/run_one.py", "--impl")):
+        r = subprocess.run([sys.executable, script, "--help"], cwd=pkg, capture_output=True, text=True, timeout=600)
+        assert r.returncode == 0 and word in r.stdout, (script, r.stderr[-500:])
+    from autotune import hw_counters as at
+    assert at is hc
