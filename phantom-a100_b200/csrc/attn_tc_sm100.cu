@@ -788,15 +788,20 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
   }
 }
 
-// Merge of the K/V parts of a launch's tail blocks. Block (tail block, Q tile, 32-column chunk); thread =
+// Merge of the K/V parts of a launch's tail blocks. Block (tail block, Q tile, 16-column chunk); thread =
 // query row. m = max_p m_p, O = sum_p 2^(m_p - m) O_p / sum_p 2^(m_p - m) l_p, summed over the parts in
-// their fixed order (results do not depend on which part ran first or where). bf16 inputs: blocks of heads
-// whose V overflows fp16 were not cut into parts (the second launch computes them whole) and are skipped.
+// their fixed order (results do not depend on which part ran first or where). All of a thread's loads (the
+// parts' (max, sum) pairs and their 16 columns of O, up to kMaxParts parts) are issued before any is used:
+// with a 32-column chunk and the parts read one after another the merge of the 4-head config-4 shard was
+// latency-bound (14.6 us for 57 MB, mostly from L2). bf16 inputs: blocks of heads whose V overflows fp16
+// were not cut into parts (the second launch computes them whole) and are skipped.
+constexpr int kMergeCols = 16;
 template <int D, bool BF16>
 __global__ void __launch_bounds__(BM)
 merge_kv_parts(const float4* __restrict__ part_o, const float2* __restrict__ part_ml, uint16_t* __restrict__ O,
                int BH, int N, int n_qblk, int group_heads, int tail_from, int P, const int* __restrict__ vflags,
                int vchunks) {
+  constexpr int kMaxP = 8;  // = kMaxParts (host side)
   asm volatile("griddepcontrol.wait;" ::: "memory");  // launched as a programmatic dependent of the attention kernel
   const int tb = blockIdx.x, g = blockIdx.y, c = blockIdx.z, r = threadIdx.x;
   int bh, qt0;
@@ -809,39 +814,49 @@ merge_kv_parts(const float4* __restrict__ part_o, const float2* __restrict__ par
   const int row = (qt0 + g) * BM + r;
   if (qt0 + g >= (N + BM - 1) / BM || row >= N) return;  // no second Q tile / past the end
   const size_t slot0 = ((size_t)tb * 2 + g) * P;
+  float2 ml[kMaxP];
+  float4 v[kMaxP][kMergeCols / 4];
+#pragma unroll
+  for (int q = 0; q < kMaxP; ++q) {
+    if (q < P) {
+      ml[q] = part_ml[(slot0 + q) * BM + r];
+      const float4* po = part_o + (slot0 + q) * (D / 4) * BM + r;
+#pragma unroll
+      for (int i = 0; i < kMergeCols / 4; ++i) v[q][i] = po[(size_t)(c * (kMergeCols / 4) + i) * BM];
+    }
+  }
   float m = -CUDART_INF_F;
-  for (int q = 0; q < P; ++q) m = fmaxf(m, part_ml[(slot0 + q) * BM + r].x);
-  float acc[32], lt = 0.f;
 #pragma unroll
-  for (int i = 0; i < 32; ++i) acc[i] = 0.f;
-  for (int q = 0; q < P; ++q) {
-    const float2 ml = part_ml[(slot0 + q) * BM + r];
-    const float w = ex2(ml.x - m);
-    lt = fmaf(w, ml.y, lt);
-    const float4* po = part_o + (slot0 + q) * (D / 4) * BM + r;
-    float4 v[8];
+  for (int q = 0; q < kMaxP; ++q)
+    if (q < P) m = fmaxf(m, ml[q].x);
+  float acc[kMergeCols], lt = 0.f;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) v[i] = po[(size_t)(c * 8 + i) * BM];  // all eight loads in flight at once
+  for (int i = 0; i < kMergeCols; ++i) acc[i] = 0.f;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      acc[4 * i] = fmaf(w, v[i].x, acc[4 * i]);
-      acc[4 * i + 1] = fmaf(w, v[i].y, acc[4 * i + 1]);
-      acc[4 * i + 2] = fmaf(w, v[i].z, acc[4 * i + 2]);
-      acc[4 * i + 3] = fmaf(w, v[i].w, acc[4 * i + 3]);
+  for (int q = 0; q < kMaxP; ++q) {
+    if (q < P) {
+      const float w = ex2(ml[q].x - m);
+      lt = fmaf(w, ml[q].y, lt);
+#pragma unroll
+      for (int i = 0; i < kMergeCols / 4; ++i) {
+        acc[4 * i] = fmaf(w, v[q][i].x, acc[4 * i]);
+        acc[4 * i + 1] = fmaf(w, v[q][i].y, acc[4 * i + 1]);
+        acc[4 * i + 2] = fmaf(w, v[q][i].z, acc[4 * i + 2]);
+        acc[4 * i + 3] = fmaf(w, v[q][i].w, acc[4 * i + 3]);
+      }
     }
   }
   const float inv_l = 1.f / lt;
-  uint32_t w[16];
+  uint32_t w[kMergeCols / 2];
 #pragma unroll
-  for (int i = 0; i < 16; ++i) w[i] = pack2<BF16>(acc[2 * i] * inv_l, acc[2 * i + 1] * inv_l);
-  uint16_t* dst = O + ((size_t)bh * N + row) * D + c * 32;
+  for (int i = 0; i < kMergeCols / 2; ++i) w[i] = pack2<BF16>(acc[2 * i] * inv_l, acc[2 * i + 1] * inv_l);
+  uint16_t* dst = O + ((size_t)bh * N + row) * D + c * kMergeCols;
   if ((reinterpret_cast<uintptr_t>(O) & 31) == 0) {
     st_global_v8(dst, w);
-    st_global_v8(dst + 16, w + 8);
   } else {
     uint4* d4 = reinterpret_cast<uint4*>(dst);
 #pragma unroll
-    for (int i = 0; i < 4; ++i) d4[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+    for (int i = 0; i < kMergeCols / 8; ++i) d4[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
   }
 }
 
@@ -984,6 +999,7 @@ struct Plan {
 // 8-GPU shard (1 full wave + 108 blocks, predicted 12.5%) runs 3.6% faster with 4 parts; parts of 8 K/V tiles
 // (config 3's 8-GPU shard) lost 24% with an in-kernel merge, hence at least 16 tiles per part.
 constexpr int kMaxParts = 8;
+static_assert(kMaxParts <= 8, "merge_kv_parts holds at most 8 parts' loads in registers");
 constexpr int kMinPartTiles = 16;
 constexpr double kMinPartGain = 0.08;
 int kv_parts(long long waves, long long r, long long grid, int n_kv) {
@@ -1141,7 +1157,7 @@ cudaError_t launch_t(const LaunchArgs& a, const Plan& p, const CUtensorMap& mq, 
     // the kernel (griddepcontrol.wait) for the whole attention grid, instead of for a launch after it
     const int n_qblk = ((a.N + tc::BM - 1) / tc::BM + 1) / 2;
     cudaLaunchConfig_t mcfg = {};
-    mcfg.gridDim = dim3(p.n_tail, 2, D / 32);
+    mcfg.gridDim = dim3(p.n_tail, 2, D / tc::kMergeCols);
     mcfg.blockDim = dim3(tc::BM);
     mcfg.stream = a.stream;
     mcfg.attrs = attr_pdl;
