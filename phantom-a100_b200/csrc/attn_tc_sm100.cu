@@ -166,16 +166,28 @@ stage_v_f16(const uint4* __restrict__ V, uint4* __restrict__ Vh, int* __restrict
   const uint4* src = V + (long long)bh * vec_per_head;
   uint4* dst = Vh + (long long)bh * vec_per_head;
   int ovf = 0;
-  for (long long i = b + threadIdx.x; i < e; i += blockDim.x) {
-    const uint4 w = src[i];
-    uint32_t in[4] = {w.x, w.y, w.z, w.w}, out[4];
+  // four 16-byte loads in flight per thread (one at a time left small calls latency-bound)
+  constexpr int kU = 4;
+  for (long long i0 = b + threadIdx.x; i0 < e; i0 += kU * (long long)blockDim.x) {
+    uint4 w[kU];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const float lo = __uint_as_float(in[j] << 16), hi = __uint_as_float(in[j] & 0xFFFF0000u);
-      ovf |= (fabsf(lo) >= 65520.f && fabsf(lo) != CUDART_INF_F) | (fabsf(hi) >= 65520.f && fabsf(hi) != CUDART_INF_F);
-      out[j] = pack2<false>(lo, hi);
+    for (int u = 0; u < kU; ++u) {
+      const long long i = i0 + (long long)u * blockDim.x;
+      if (i < e) w[u] = src[i];
     }
-    dst[i] = make_uint4(out[0], out[1], out[2], out[3]);
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      const long long i = i0 + (long long)u * blockDim.x;
+      if (i >= e) continue;
+      uint32_t in[4] = {w[u].x, w[u].y, w[u].z, w[u].w}, out[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float lo = __uint_as_float(in[j] << 16), hi = __uint_as_float(in[j] & 0xFFFF0000u);
+        ovf |= (fabsf(lo) >= 65520.f && fabsf(lo) != CUDART_INF_F) | (fabsf(hi) >= 65520.f && fabsf(hi) != CUDART_INF_F);
+        out[j] = pack2<false>(lo, hi);
+      }
+      dst[i] = make_uint4(out[0], out[1], out[2], out[3]);
+    }
   }
   ovf = __syncthreads_or(ovf);
   if (threadIdx.x == 0) {
