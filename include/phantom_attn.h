@@ -140,8 +140,8 @@ int phantom_attn_wait_expiry_probe(void* stream);
 /*
  * Device memory the library takes besides the caller's tensors, for peak-memory reporting (the reference
  * benchmark recorded peak_memory_mb, bench/benchmark.py:96-102; its kernels allocated through torch).
- * The tensor-core entry points take per-launch scratch (work counter, fp16 copy of V for bf16 inputs,
- * K/V-part partials) from a stream-ordered pool per device. *high_water = the most scratch in use at once
+ * The tensor-core entry points take per-call scratch (work counters and, for bf16 inputs, the overflow word,
+ * the fp16 copy of V and its overflow flags; K/V-part partials) from a stream-ordered pool per device. *high_water = the most scratch in use at once
  * on the current device since the last reset, *reserved = bytes the pool holds now (it keeps freed
  * blocks for reuse); both 0 before any call needed scratch. reset = 1 restarts the high-water mark.
  * phantom_attn_fused_tc_noalloc uses its static array instead and is not counted.
