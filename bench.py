@@ -524,7 +524,7 @@ def main():
                      "kernel_mcycles_at_median_sm_clock": avg_kernel_ms * sm_mhz * 1e-3 if avg_kernel_ms and sm_mhz else None},
         "e2e": {"value": total_flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms, "steps": e2e_steps,
-                "path": "pinned host -> cuda_attn.fused_tc_host (public API; copies overlapped with the kernel over head chunks: 8 full, the last cut in halves) -> pinned host", "matches_value_run": e2e_same},
+                "path": "pinned host -> cuda_attn.fused_tc_host (public API; copies overlapped with the kernel over head chunks: at most 8 full ones of at least 32 MiB per input tensor, the last cut in halves down to 8 MiB) -> pinned host", "matches_value_run": e2e_same},
         "memory": dict(peak_mem, inputs_mb=3 * q.numel() * q.element_size() / 2**20,
                        note="one cuda_attn.fused_tc call on this rank's heads: O from torch plus the library's "
                             "scratch (bf16: fp16 copy of V; multi-wave: work counter; K/V parts: partials)"),

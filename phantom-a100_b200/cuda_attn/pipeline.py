@@ -10,7 +10,11 @@ and the two directions overlap each other. Three slots let the copy of chunk i+2
 output is still in flight (the output copy shares the link with the input copies). The last full chunk is
 cut into halves down to two heads (... per, per/2, ..., 2, 2), so that the work left after the last input
 copy, the last chunk's attention and output copy, is small; back-to-back calls also overlap it with the
-next call's first input copies (measured on config 4: 8.48 -> 8.13 ms per call). Each chunk runs the same C-ABI entry point as
+next call's first input copies (measured on config 4: 8.48 -> 8.13 ms per call). Chunks are also kept
+large in bytes: a full chunk copies at least MIN_CHUNK_BYTES of each input tensor and the halving stops
+at MIN_TAIL_BYTES, because small copies run far below the link rate (config 2's 2 MiB and 256 KiB copies
+ran at ~30 GB/s: 1.59 ms per call in 11 chunks, 1.30-1.38 ms in two; config 3 8.41 -> 8.10 ms; config 4,
+whose chunks were already 16 MiB, unchanged). Each chunk runs the same C-ABI entry point as
 fused_tc, with the tail's K/V parts turned off (phantom_attn_set_kv_parts(0) on this thread for the
 duration of the call): the call is bound by the host link, not by the kernel's last wave, and every query
 block then runs over its whole K/V range, so the result equals a device-resident fused_tc call without
@@ -57,21 +61,30 @@ def _streams(device: torch.device):
 
 
 MIN_TAIL_HEADS = 2  # a one-head chunk's three 4 MiB input copies ran at ~35 GB/s (config 4), two heads' at ~47
+MIN_CHUNK_BYTES = 32 << 20  # per input tensor, full chunks
+MIN_TAIL_BYTES = 8 << 20  # per input tensor, the halved tail chunks
 
 
-def chunk_plan(bh: int, chunks: int) -> list[int]:
+def chunk_plan(bh: int, chunks: int, head_bytes: int = 0, min_chunk_bytes: int = 0,
+               min_tail_bytes: int = 0) -> list[int]:
     """Head counts of the chunks: full chunks of ceil(bh / chunks) heads, then the last one cut into
     halves down to chunks of MIN_TAIL_HEADS (4 -> 2, 2; 8 -> 4, 2, 2), so the tail after the last input
-    copy is small. chunks <= 1: one chunk of all heads (no pipelining)."""
+    copy is small. With head_bytes (one head of one input tensor) given, a full chunk also holds at least
+    min_chunk_bytes and the halving stops at min_tail_bytes per input tensor. chunks <= 1: one chunk of all
+    heads (no pipelining)."""
     if chunks <= 1:
         return [bh]
     per = max(1, math.ceil(bh / chunks))
+    tail_min = MIN_TAIL_HEADS
+    if head_bytes > 0:
+        per = max(per, math.ceil(min_chunk_bytes / head_bytes))
+        tail_min = max(tail_min, math.ceil(min_tail_bytes / head_bytes))
     sizes = []
     left = bh
     while left > per:
         sizes.append(per)
         left -= per
-    while left >= 2 * MIN_TAIL_HEADS:
+    while left >= 2 * tail_min:
         half = left // 2
         sizes.append(left - half)
         left = half
@@ -82,7 +95,8 @@ def chunk_plan(bh: int, chunks: int) -> list[int]:
 
 def fused_tc_host(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool = False,
                   out: torch.Tensor | None = None, chunks: int = 8, device: int | torch.device | None = None,
-                  synchronize: bool = True, trace: list | None = None) -> torch.Tensor:
+                  synchronize: bool = True, trace: list | None = None, min_chunk_bytes: int = MIN_CHUNK_BYTES,
+                  min_tail_bytes: int = MIN_TAIL_BYTES) -> torch.Tensor:
     """fused_tc for (B, H, N, d) CPU tensors (pin them for overlap; pageable memory works but serialises
     the copies). Returns O as a CPU tensor of the input dtype (`out` if given, pinned otherwise). With
     synchronize=False the call returns once the work is queued; the current CUDA stream of `device` is
@@ -94,6 +108,10 @@ def fused_tc_host(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: boo
     this thread that is still being copied back, which the input copies wait for (chained calls, e.g.
     one call's O as the next call's Q). The output copies wait for the current stream, so GPU work queued
     on it before the call that still reads `out` is not overwritten.
+
+    chunks: full chunks at most (heads are cut into ceil(B*H / chunks)-head chunks, each also holding at
+    least min_chunk_bytes of each input tensor; the last is halved down to min_tail_bytes; pass 0 for both
+    to chunk by head count alone).
 
     trace: if a list is given, one record per chunk is appended - {"heads", "h2d", "attend", "d2h"}, each
     a (start, end) pair of CUDA events (timing-enabled) on that stage's stream (cuda_attn.timeline)."""
@@ -114,7 +132,7 @@ def fused_tc_host(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: boo
     if out is None:
         out = torch.empty(q.shape, dtype=q.dtype, pin_memory=True)
     hq, hk, hv, ho = (x.view(BH, N, d) for x in (q, k, v, out))
-    sizes = chunk_plan(BH, chunks)
+    sizes = chunk_plan(BH, chunks, N * d * q.element_size(), min_chunk_bytes, min_tail_bytes)
     per = sizes[0]
     n_slots = min(3, len(sizes))
     lib = _lib()

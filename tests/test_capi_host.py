@@ -128,3 +128,21 @@ def test_host_pipeline_chunk_plan(bh, chunks):
     assert all(s <= per for s in sizes)
     assert sizes == sorted(sizes, reverse=True)
     assert sizes[-1] <= 3  # halving stops once fewer than four heads are left
+
+
+@pytest.mark.parametrize("bh,head_bytes,expect", [
+    (128, 128 << 10, [64, 64]),                   # config 2: 16 MiB per tensor in all, no full 32 MiB chunk
+    (128, 1 << 20, [32, 32, 32, 16, 8, 8]),       # config 3
+    (32, 4 << 20, [8, 8, 8, 4, 2, 2]),            # config 4
+    (4, 4 << 20, [2, 2]),                         # config 4's 8-GPU shard
+    (16, 1 << 20, [8, 8]),                        # config 3's 8-GPU shard
+    (3, 64 << 20, [1, 1, 1]),                     # heads above the floor: chunk by count
+    (1, 1 << 10, [1]),
+])
+def test_host_pipeline_chunk_plan_byte_floors(bh, head_bytes, expect):
+    """With a head's bytes given, full chunks hold at least MIN_CHUNK_BYTES of each input tensor and the
+    tail halving stops at MIN_TAIL_BYTES (small copies run far below the host link's rate)."""
+    from cuda_attn.pipeline import MIN_CHUNK_BYTES, MIN_TAIL_BYTES, chunk_plan
+    sizes = chunk_plan(bh, 8, head_bytes, MIN_CHUNK_BYTES, MIN_TAIL_BYTES)
+    assert sizes == expect
+    assert sum(sizes) == bh and sizes == sorted(sizes, reverse=True)

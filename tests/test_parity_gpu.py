@@ -333,7 +333,7 @@ def test_two_threads_through_the_host_pipeline(capi):
     def work(i):
         try:
             for _ in range(2):
-                results[i] = cuda_attn.fused_tc_host(*host[i], chunks=3)
+                results[i] = cuda_attn.fused_tc_host(*host[i], chunks=3, min_chunk_bytes=0, min_tail_bytes=0)
         except Exception as e:  # reported by the main thread
             errors.append(e)
 
@@ -361,8 +361,8 @@ def test_host_pipeline_chained_calls_without_synchronising(capi):
     h1 = torch.empty(q.shape, dtype=q.dtype, pin_memory=True)
     h2 = torch.empty(q.shape, dtype=q.dtype, pin_memory=True)
     for _ in range(2):
-        cuda_attn.fused_tc_host(hq, hk, hv, out=h1, chunks=4, synchronize=False)
-        cuda_attn.fused_tc_host(h1, hk, hv, out=h2, chunks=4, synchronize=False)
+        cuda_attn.fused_tc_host(hq, hk, hv, out=h1, chunks=4, synchronize=False, min_chunk_bytes=0, min_tail_bytes=0)
+        cuda_attn.fused_tc_host(h1, hk, hv, out=h2, chunks=4, synchronize=False, min_chunk_bytes=0, min_tail_bytes=0)
     torch.cuda.synchronize()
     assert torch.equal(h1, o1.cpu()) and torch.equal(h2, o2.cpu())
 
@@ -433,12 +433,34 @@ def test_causal_full_size(capi, dtype):
 @pytest.mark.parametrize("chunks", [1, 3, 8])
 def test_host_pipeline_equals_device_call(capi, dtype, chunks):
     """fused_tc_host streams head chunks through the GPU; heads are independent, so the result must equal
-    the device-resident call bit for bit, for any chunking (including a ragged last chunk)."""
+    the device-resident call bit for bit, for any chunking (including a ragged last chunk; the byte floors
+    are turned off so that these small heads are chunked by count)."""
     import cuda_attn
     q, k, v = make_qkv(2, 5, 700, 128, dtype, seed=31)
     o_dev = torch.empty_like(q)
     capi.fused_tc(q, k, v, o_dev, causal=True)
     hq, hk, hv = (x.cpu().pin_memory() for x in (q, k, v))
-    o_host = cuda_attn.fused_tc_host(hq, hk, hv, causal=True, chunks=chunks)
+    o_host = cuda_attn.fused_tc_host(hq, hk, hv, causal=True, chunks=chunks, min_chunk_bytes=0, min_tail_bytes=0)
     assert not o_host.is_cuda and o_host.dtype == dtype
+    assert torch.equal(o_host, o_dev.cpu())
+
+
+def test_host_pipeline_byte_floors_equal_device_call(capi):
+    """With the default byte floors, 12 heads of 2 MiB per tensor (N = 8192, d = 128) run as two 6-head
+    chunks (a full chunk would need 16 heads for 32 MiB; the halving stops at 4 heads = 8 MiB): the trace
+    shows the plan, and the result equals the device-resident call without K/V parts bit for bit (the
+    pipeline turns them off; this shape's device call would cut its last wave into parts)."""
+    import cuda_attn
+    q, k, v = make_qkv(1, 12, 8192, 128, torch.float16, seed=32)
+    o_dev = torch.empty_like(q)
+    was = capi.get_kv_parts()
+    capi.set_kv_parts(False)
+    try:
+        capi.fused_tc(q, k, v, o_dev)
+    finally:
+        capi.set_kv_parts(was)
+    hq, hk, hv = (x.cpu().pin_memory() for x in (q, k, v))
+    trace = []
+    o_host = cuda_attn.fused_tc_host(hq, hk, hv, trace=trace)
+    assert [r["heads"] for r in trace] == [6, 6]
     assert torch.equal(o_host, o_dev.cpu())
