@@ -895,6 +895,14 @@ __global__ void __launch_bounds__(32, 1) wait_expiry_probe(int* __restrict__ sta
   if (threadIdx.x == 0 && !first && status2 != nullptr) atomicOr(status2, kErrProbeWait);
 }
 
+// Zeroes the persistent CTAs' work counter of an fp16 call (bf16 calls have the staging kernel do it). A kernel
+// rather than a memset, so that the stream's programmatic-launch chain stays unbroken: it waits for the work
+// before it, and the attention kernel after it is scheduled as it exits and waits for it in turn.
+__global__ void __launch_bounds__(32, 1) zero_counter(int* __restrict__ ctr) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  if (threadIdx.x == 0) ctr[0] = 0;
+}
+
 }  // namespace tc
 
 // ------------------------------------------------------------------------------------ host side
@@ -1202,15 +1210,26 @@ cudaError_t launch_t(const LaunchArgs& a, const Plan& p, const CUtensorMap& mq, 
   return e;
 }
 
-// One call in the scratch `s`: zero the work counter (fp16: a memset; bf16: the staging kernel does it), stage
+// One call in the scratch `s`: zero the work counter (fp16: zero_counter; bf16: the staging kernel does it), stage
 // V as fp16 (bf16), run the attention kernel.
 template <int D>
 cudaError_t run_d(const LaunchArgs& a, const Plan& p, const CUtensorMap& mq, const CUtensorMap& mk,
                   const CUtensorMap& mv, const Scratch& s, int dev) {
   const bool bf16 = a.dtype == PHANTOM_ATTN_BF16;
-  if (const size_t cb = counters_used(p, bf16); cb && !bf16) {
-    cudaError_t e = cudaMemsetAsync(s.ctr, 0, cb, a.stream);
+  if (counters_used(p, bf16) && !bf16) {
+    cudaLaunchConfig_t zcfg = {};
+    zcfg.gridDim = dim3(1);
+    zcfg.blockDim = dim3(32);
+    zcfg.stream = a.stream;
+    cudaLaunchAttribute zpdl[1];
+    zpdl[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    zpdl[0].val.programmaticStreamSerializationAllowed = 1;
+    zcfg.attrs = zpdl;
+    zcfg.numAttrs = 1;
+    cudaError_t e = cudaLaunchKernelEx(&zcfg, tc::zero_counter, s.ctr);
     if (e != cudaSuccess) return e;
+    note_launch();
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
   }
   if (!bf16) return launch_t<D, false>(a, p, mq, mk, mv, mv, s, dev);
   const long long vec_per_head = (long long)a.N * D / 8;
