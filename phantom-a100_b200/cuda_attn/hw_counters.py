@@ -165,9 +165,10 @@ def is_overflow_launch(name: str) -> bool:
 
 def calls(launches: list[dict], last: str = ATTENTION_KERNEL) -> list[list[dict]]:
     """Group launches into forward calls: each group ends with the main launch of the attention kernel (a
-    bf16 call is stage_v_f16 then attn_fwd_tc), followed by the merge_kv_parts launch when the call cut its
-    last wave into K/V parts and, for bf16, the attention launch for fp16-overflow heads. Launches after the
-    last main attention launch form no call."""
+    bf16 call is stage_v_f16 then attn_fwd_tc; an fp16 call with more units than CTAs is zero_counter then
+    attn_fwd_tc, when the capture's filter takes zero_counter in), followed by the merge_kv_parts launch
+    when the call cut its last wave into K/V parts and, for bf16, the attention launch for fp16-overflow
+    heads. Launches after the last main attention launch form no call."""
     groups, cur = [], []
     for rec in launches:
         if (MERGE_KERNEL in rec["kernel"] or is_overflow_launch(rec["kernel"])) and groups and not cur:

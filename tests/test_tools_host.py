@@ -107,6 +107,12 @@ def test_calls_attach_the_overflow_heads_launch():
     assert not hc.is_overflow_launch("attn_fwd_tc<128, true, false, false>") and not hc.is_overflow_launch("stage_v_f16")
 
 
+def test_calls_start_an_fp16_call_at_its_counter_zeroing():
+    ls = [launch("tc::zero_counter(int*)", 1), launch("void attn_fwd_tc<64, 0, 0, 0>(...)", 2),
+          launch("void attn_fwd_tc<64, 0, 0, 0>(...)", 3)]
+    assert [[r[T] for r in g] for g in hc.calls(ls)] == [[1, 2], [3]]
+
+
 def test_calls_attach_the_merge_of_k_v_parts():
     ls = [launch("tc::stage_v_f16", 1), launch("tc::attn_fwd_tc<128, true, true>", 2),
           launch("tc::merge_kv_parts<128, true>", 3), launch("tc::attn_fwd_tc<128, false, false>", 4)]
